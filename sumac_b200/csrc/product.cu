@@ -1,0 +1,223 @@
+// product.cu — tensor maps, the (Dp, precision) configuration table and launchers of the fused
+// ReLU product / reduce kernel (relu_product.cuh).
+#include "kernels.cuh"
+#include "relu_product.cuh"
+
+namespace sb {
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D fp32 map over a row-major [rows][inner] array with `ld` floats per row. Out-of-range boxes
+// read as zero.
+static bool make_map(CUtensorMap* m, const float* base, uint64_t inner, uint64_t rows, uint64_t ld,
+                     uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle sw) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t gdim[2] = {inner, rows};
+  cuuint64_t gstride[1] = {ld * sizeof(float)};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estride[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), gdim, gstride,
+                  box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+struct ProdCfgRt {
+  int bn, stages;
+  bool ok;
+};
+
+static ProdCfgRt product_cfg(int Dp, bool x3) {
+  if (!x3) {
+    switch (Dp) {
+      case 16: return {128, 6, true};
+      case 32: return {128, 4, true};
+      case 64: return {128, 2, true};
+      case 128: return {64, 2, true};
+    }
+  } else {
+    switch (Dp) {
+      case 16: return {64, 6, true};
+      case 32: return {64, 4, true};
+      case 64: return {64, 2, true};
+    }
+  }
+  return {0, 0, false};
+}
+
+static ProdCfgRt reduce_cfg(int Dp, bool x3) {
+  if (!x3) {
+    switch (Dp) {
+      case 16: return {128, 6, true};
+      case 32: return {128, 4, true};
+      case 64: return {128, 3, true};
+      case 128: return {64, 2, true};
+      case 256: return {32, 2, true};
+    }
+  } else {
+    switch (Dp) {
+      case 16: return {128, 4, true};
+      case 32: return {128, 3, true};
+      case 64: return {64, 3, true};
+      case 128: return {32, 2, true};
+    }
+  }
+  return {0, 0, false};
+}
+
+bool product_supported(int Dp, bool x3) { return product_cfg(Dp, x3).ok; }
+bool reduce_supported(int Dp, bool x3) { return reduce_cfg(Dp, x3).ok; }
+
+// Split-K: when there are fewer row tiles than SMs, split the chunk range so that every SM gets
+// work, keeping at least ~4 chunks per split and no empty split.
+static void plan_splits(int64_t M, int64_t N, int bn, int num_sms, int* splits, int* cps,
+                        int* n_chunks, int* n_tiles) {
+  const int64_t tiles = (M + 127) / 128;
+  const int64_t nc = (N + bn - 1) / bn;
+  int64_t s = 1;
+  if (tiles < num_sms) {
+    s = (num_sms + tiles - 1) / tiles;
+    int64_t max_s = nc / 4;
+    if (max_s < 1) max_s = 1;
+    if (s > max_s) s = max_s;
+  }
+  int64_t c = (nc + s - 1) / s;
+  s = (nc + c - 1) / c;
+  *splits = (int)s;
+  *cps = (int)c;
+  *n_chunks = (int)nc;
+  *n_tiles = (int)tiles;
+}
+
+int product_split_count(int64_t M, int64_t N, int Dp, bool x3, int num_sms) {
+  ProdCfgRt c = product_cfg(Dp, x3);
+  if (!c.ok) return 0;
+  int s, cps, nc, nt;
+  plan_splits(M, N, c.bn, num_sms, &s, &cps, &nc, &nt);
+  return s;
+}
+
+template <int DP, int BN, int STAGES, bool X3, bool REDUCE>
+static int run_kernel(const CUtensorMap& mx, const CUtensorMap& mfh, const CUtensorMap& mfl,
+                      const CUtensorMap& mch, const CUtensorMap& mcl, const ProductParams& p,
+                      int grid, cudaStream_t stream) {
+  using Cfg = ProductCfg<DP, BN, STAGES, X3, REDUCE>;
+  auto kern = relu_product_kernel<DP, BN, STAGES, X3, REDUCE>;
+  cudaError_t e =
+      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+  if (e != cudaSuccess) return (int)e;
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(mx, mfh, mfl, mch, mcl, p);
+  return (int)cudaGetLastError();
+}
+
+#define SB_PRODUCT_CASE(DPV, BNV, STV, X3V, REDV)                                              \
+  if (Dp == DPV && bn == BNV && stages == STV && x3 == X3V)                                    \
+    return run_kernel<DPV, BNV, STV, X3V, REDV>(mx, mfh, mfl, mch, mcl, p, grid, stream);
+
+static int dispatch_product(int Dp, int bn, int stages, bool x3, const CUtensorMap& mx,
+                            const CUtensorMap& mfh, const CUtensorMap& mfl, const CUtensorMap& mch,
+                            const CUtensorMap& mcl, const ProductParams& p, int grid,
+                            cudaStream_t stream) {
+  SB_PRODUCT_CASE(16, 128, 6, false, false)
+  SB_PRODUCT_CASE(32, 128, 4, false, false)
+  SB_PRODUCT_CASE(64, 128, 2, false, false)
+  SB_PRODUCT_CASE(128, 64, 2, false, false)
+  SB_PRODUCT_CASE(16, 64, 6, true, false)
+  SB_PRODUCT_CASE(32, 64, 4, true, false)
+  SB_PRODUCT_CASE(64, 64, 2, true, false)
+  return -1;
+}
+
+static int dispatch_reduce(int Dp, int bn, int stages, bool x3, const CUtensorMap& mx,
+                           const CUtensorMap& mfh, const CUtensorMap& mfl, const CUtensorMap& mch,
+                           const CUtensorMap& mcl, const ProductParams& p, int grid,
+                           cudaStream_t stream) {
+  SB_PRODUCT_CASE(16, 128, 6, false, true)
+  SB_PRODUCT_CASE(32, 128, 4, false, true)
+  SB_PRODUCT_CASE(64, 128, 3, false, true)
+  SB_PRODUCT_CASE(128, 64, 2, false, true)
+  SB_PRODUCT_CASE(256, 32, 2, false, true)
+  SB_PRODUCT_CASE(16, 128, 4, true, true)
+  SB_PRODUCT_CASE(32, 128, 3, true, true)
+  SB_PRODUCT_CASE(64, 64, 3, true, true)
+  SB_PRODUCT_CASE(128, 32, 2, true, true)
+  return -1;
+}
+#undef SB_PRODUCT_CASE
+
+static CUtensorMapSwizzle row_swizzle(int Dp) {
+  return Dp * 4 >= 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+}
+
+int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float* Flo,
+                        const float* Cthi, const float* Ctlo, int64_t ldct, int64_t N, int Dp,
+                        bool x3, float* ws, int* err, int num_sms, unsigned long long timeout_ns,
+                        cudaStream_t stream) {
+  ProdCfgRt c = product_cfg(Dp, x3);
+  if (!c.ok) return -1;
+  if (M <= 0 || N <= 0 || M >= INT32_MAX || N >= INT32_MAX) return -5;
+  const uint32_t box_k = Dp * 4 <= 128 ? Dp : 32;
+  CUtensorMap mx, mfh, mfl, mch, mcl;
+  const CUtensorMapSwizzle sw = row_swizzle(Dp);
+  if (!make_map(&mx, X, Dp, M, Dp, box_k, 128, sw)) return -6;
+  if (!make_map(&mfh, Fhi, Dp, N, Dp, box_k, c.bn, sw)) return -6;
+  if (!make_map(&mfl, x3 ? Flo : Fhi, Dp, N, Dp, box_k, c.bn, sw)) return -6;
+  if (!make_map(&mch, Cthi, N, Dp, ldct, 32, Dp, CU_TENSOR_MAP_SWIZZLE_128B)) return -6;
+  if (!make_map(&mcl, x3 ? Ctlo : Cthi, N, Dp, ldct, 32, Dp, CU_TENSOR_MAP_SWIZZLE_128B)) return -6;
+  ProductParams p;
+  p.M = (int)M;
+  p.N = (int)N;
+  plan_splits(M, N, c.bn, num_sms, &p.splits, &p.chunks_per_split, &p.n_chunks, &p.n_tiles);
+  p.ws = ws;
+  p.partials = nullptr;
+  p.err = err;
+  p.timeout_ns = timeout_ns;
+  const int64_t items = (int64_t)p.n_tiles * p.splits;
+  const int grid = (int)(items < num_sms ? items : num_sms);
+  return dispatch_product(Dp, c.bn, c.stages, x3, mx, mfh, mfl, mch, mcl, p, grid, stream);
+}
+
+int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float* Flo, int64_t N,
+                       int Dp, bool x3, double* partials, int* grid_out, int* err, int num_sms,
+                       unsigned long long timeout_ns, cudaStream_t stream) {
+  ProdCfgRt c = reduce_cfg(Dp, x3);
+  if (!c.ok) return -1;
+  if (M <= 0 || N <= 0 || M >= INT32_MAX || N >= INT32_MAX) return -5;
+  const uint32_t box_k = Dp * 4 <= 128 ? Dp : 32;
+  CUtensorMap mx, mfh, mfl;
+  const CUtensorMapSwizzle sw = row_swizzle(Dp);
+  if (!make_map(&mx, X, Dp, M, Dp, box_k, 128, sw)) return -6;
+  if (!make_map(&mfh, Fhi, Dp, N, Dp, box_k, c.bn, sw)) return -6;
+  if (!make_map(&mfl, x3 ? Flo : Fhi, Dp, N, Dp, box_k, c.bn, sw)) return -6;
+  ProductParams p;
+  p.M = (int)M;
+  p.N = (int)N;
+  plan_splits(M, N, c.bn, num_sms, &p.splits, &p.chunks_per_split, &p.n_chunks, &p.n_tiles);
+  p.ws = nullptr;
+  p.partials = partials;
+  p.err = err;
+  p.timeout_ns = timeout_ns;
+  const int64_t items = (int64_t)p.n_tiles * p.splits;
+  const int grid = (int)(items < num_sms ? items : num_sms);
+  *grid_out = grid;
+  return dispatch_reduce(Dp, c.bn, c.stages, x3, mx, mfh, mfl, mfh, mfh, p, grid, stream);
+}
+
+}  // namespace sb
