@@ -1,0 +1,183 @@
+"""Parity of the CUDA kernels (through the C ABI) with the CPU oracle on the same seeded inputs.
+
+Tolerances: relative to max|reference|, 1e-5 in 3xTF32 mode (fp32 accuracy) and 2e-3 in TF32
+mode; the CSR builder must be bit-exact.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import sumac_oracle as orc
+from sumac_b200 import _native, ops
+from tests.helpers import host_csr, pad, random_edges, rel_err, to_dev
+
+pytestmark = pytest.mark.gpu
+
+TOL = {ops.SUMAC_3XTF32: 1e-5, ops.SUMAC_TF32: 2e-3}
+PRECS = [ops.SUMAC_3XTF32, ops.SUMAC_TF32]
+
+
+def _supported(D, prec):
+    return not (prec == ops.SUMAC_3XTF32 and ops.padded_rank(D) > 64)
+
+
+@pytest.mark.parametrize("prec", PRECS)
+@pytest.mark.parametrize("D,N,M", [(8, 250, 3000), (13, 77, 1000), (16, 250, 25000), (17, 250, 2000),
+                                   (32, 250, 25000), (64, 300, 5000), (128, 250, 2000),
+                                   (16, 5000, 300), (16, 3, 130)])
+def test_relu_bat_c(D, N, M, prec):
+    if not _supported(D, prec):
+        pytest.skip("3xTF32 product is built for rank <= 64")
+    rng = np.random.default_rng(D * 1000 + N)
+    A = rng.standard_normal((N, D)).astype(np.float32)
+    B = rng.standard_normal((M, D)).astype(np.float32)
+    C = rng.standard_normal((N, D)).astype(np.float32)
+    Y = ops.relu_bat_c(to_dev(A), to_dev(B), to_dev(C), prec).cpu().numpy()
+    _native.raise_device_error(0)
+    assert rel_err(Y, orc.relu_bat_c(A, B, C)) < TOL[prec]
+
+
+@pytest.mark.parametrize("prec", PRECS)
+@pytest.mark.parametrize("D", [13, 16, 32, 64, 128, 256])
+def test_relu_bat_reduce(D, prec):
+    if prec == ops.SUMAC_3XTF32 and D > 128:
+        pytest.skip("3xTF32 reduce is built for rank <= 128")
+    rng = np.random.default_rng(D)
+    A = rng.standard_normal((25000, D)).astype(np.float32)
+    B = rng.standard_normal((250, D)).astype(np.float32)
+    got = ops.relu_bat_reduce(to_dev(A), to_dev(B), prec).cpu().numpy()
+    _native.raise_device_error(0)
+    ref = orc.relu_bat_reduce(A, B)
+    np.testing.assert_allclose(got, ref, rtol=TOL[prec] * 10)
+
+
+def test_relu_bat_c_golden(golden):
+    for tag in "abc":
+        g = golden(f"relu_bat_c_{tag}")
+        Y = ops.relu_bat_c(to_dev(g["A"]), to_dev(g["B"]), to_dev(g["C"]), ops.SUMAC_3XTF32)
+        assert rel_err(Y.cpu().numpy(), g["Y"]) < 1e-5
+
+
+@pytest.mark.parametrize("prec", PRECS)
+@pytest.mark.parametrize("d,N,M,nnz", [(16, 1393, 5000, 20000), (8, 200, 700, 3000),
+                                       (32, 300, 4000, 50000), (64, 100, 129, 500)])
+def test_masked_product(d, N, M, nnz, prec):
+    rng = np.random.default_rng(d + N)
+    Dp = ops.padded_rank(d)
+    X = rng.standard_normal((M, d)).astype(np.float32)
+    F = rng.standard_normal((N, d)).astype(np.float32)
+    C = rng.standard_normal((N, d)).astype(np.float32)
+    fi, oj, v = random_edges(rng, N, M, nnz)
+    rowptr, ent = host_csr(fi, oj, v, M)
+    Y = ops.masked_product(to_dev(pad(X, Dp)), to_dev(pad(F, Dp)), to_dev(pad(C, Dp)),
+                           to_dev(rowptr), to_dev(ent), prec).cpu().numpy()[:, :d]
+    _native.raise_device_error(0)
+    ref = orc.masked_residual(F, X, fi, oj, v) @ C.astype(np.float64)
+    assert rel_err(Y, ref) < TOL[prec]
+
+
+@pytest.mark.parametrize("m_fixed,M,nb,nnz", [(57, 40, 5, 300), (1000, 777, 13, 40000),
+                                              (5000, 3000, 100, 200000), (64, 9, 64, 0),
+                                              (300, 5000, 7, 2000)])
+def test_block_csr_bit_exact(m_fixed, M, nb, nnz):
+    rng = np.random.default_rng(m_fixed + nb)
+    fi, oj, v = random_edges(rng, m_fixed, M, nnz)
+    perm = rng.permutation(m_fixed)
+    order = np.argsort(oj, kind="stable")
+    rowptr, ent = ops.block_csr_build(to_dev(perm), nb, to_dev(fi[order], torch.int32),
+                                      to_dev(oj[order], torch.int32), to_dev(v[order]), M)
+    rp_ref, loc_ref, v_ref = orc.block_csr(perm, fi, oj, v, nb, M)
+    np.testing.assert_array_equal(rowptr.cpu().numpy(), rp_ref)
+    if nnz:
+        e = ent.cpu().numpy()
+        np.testing.assert_array_equal(e[:, 0], loc_ref)
+        np.testing.assert_array_equal(e[:, 1], v_ref.view(np.int32))
+
+
+@pytest.mark.parametrize("prec", PRECS)
+@pytest.mark.parametrize("d,m_fixed,b,M,nnz", [(16, 5000, 1393, 4000, 30000), (6, 400, 100, 90, 900),
+                                               (32, 3000, 300, 2500, 20000), (64, 2000, 500, 700, 5000)])
+def test_salsa_block_update(d, m_fixed, b, M, nnz, prec):
+    rng = np.random.default_rng(d + b)
+    Dp = ops.padded_rank(d)
+    F = rng.standard_normal((m_fixed, d)).astype(np.float32)
+    X = (0.3 * rng.standard_normal((M, d))).astype(np.float32)
+    dX = (0.05 * rng.standard_normal((M, d))).astype(np.float32)
+    rows = rng.choice(m_fixed, size=b, replace=False)
+    li, oj, v = random_edges(rng, b, M, nnz)
+    rowptr, ent = host_csr(li, oj, v, M)
+    mu, lr, step = 0.7, 0.1, 5
+    unbias = np.float32(1.0) - np.float32(mu) ** np.float32(step)
+    Xd, dXd = to_dev(pad(X, Dp)), to_dev(pad(dX, Dp))
+    ops.salsa_block_update(to_dev(pad(F, Dp)), to_dev(rows), Xd, dXd, d, to_dev(rowptr),
+                           to_dev(ent), mu, lr, to_dev(np.array([unbias], np.float32)), prec)
+    _native.raise_device_error(0)
+    A_I = F[rows].astype(np.float64)
+    Bn, dBn = orc.lsq_update(A_I, X, orc.pinv_t(A_I), dX, li, oj, v, mu, float(unbias), lr)
+    tol = 1e-4 if prec == ops.SUMAC_3XTF32 else 3e-3
+    assert rel_err(dXd.cpu().numpy()[:, :d], dBn) < tol
+    assert rel_err(Xd.cpu().numpy()[:, :d], Bn) < tol
+    assert np.all(Xd.cpu().numpy()[:, d:] == 0)
+
+
+@pytest.mark.parametrize("prec", PRECS)
+@pytest.mark.parametrize("d,m,n,b,nnz", [(8, 2000, 1500, 2000, 40000), (16, 900, 3000, 300, 20000),
+                                         (32, 500, 700, 129, 3000)])
+def test_gd_block_grad(d, m, n, b, nnz, prec):
+    rng = np.random.default_rng(d + m)
+    Dp = ops.padded_rank(d)
+    A = (0.5 * rng.standard_normal((m, d))).astype(np.float32)
+    B = (0.5 * rng.standard_normal((n, d))).astype(np.float32)
+    rows = rng.choice(m, size=b, replace=False)
+    li, cj, v = random_edges(rng, b, n, nnz)
+    rp_b, ent_b = host_csr(li, cj, v, n)        # by column j, entries local i
+    rp_a, ent_a = host_csr(cj, li, v, b)        # by local row i, entries j
+    gA = torch.zeros((m, Dp), device="cuda")
+    gB = torch.zeros((n, Dp), device="cuda")
+    ops.gd_block_grad(to_dev(pad(A, Dp)), to_dev(pad(B, Dp)), d, to_dev(rows), to_dev(rp_b),
+                      to_dev(ent_b), to_dev(rp_a), to_dev(ent_a), gA, gB, 0, prec)
+    _native.raise_device_error(0)
+    _, gAI_ref, gB_ref = orc.gd_block_grad(A[rows], B, li, cj, v)
+    tol = TOL[prec] * 5
+    assert rel_err(gA.cpu().numpy()[rows, :d], gAI_ref) < tol
+    assert rel_err(gB.cpu().numpy()[:, :d], gB_ref) < tol
+    mask = np.ones(m, bool)
+    mask[rows] = False
+    assert np.all(gA.cpu().numpy()[mask] == 0)
+
+
+@pytest.mark.parametrize("prec", PRECS)
+def test_eval_terms(prec, golden):
+    g = golden("metrics")
+    d = g["A"].shape[1]
+    Dp = ops.padded_rank(d)
+    idx = g["S_index"]
+    out = ops.eval_terms(to_dev(pad(g["A"], Dp)), to_dev(pad(g["B"], Dp)), d,
+                         to_dev(idx[0], torch.int32), to_dev(idx[1], torch.int32),
+                         to_dev(g["S_value"]), precision=prec).cpu().numpy()
+    ref = orc.eval_terms(g["A"], g["B"], idx, g["S_value"])
+    np.testing.assert_allclose(out, ref, rtol=TOL[prec] * 10, atol=1e-9)
+    np.testing.assert_allclose(orc.metrics_from_terms(out), [g["rmse"], g["jacc"], g["cost"]],
+                               rtol=1e-4)
+
+
+def test_adam_matches_oracle():
+    rng = np.random.default_rng(0)
+    n = 10007
+    p, g = rng.standard_normal(n).astype(np.float32), rng.standard_normal(n).astype(np.float32)
+    m, v = np.zeros(n, np.float32), np.zeros(n, np.float32)
+    pd, gd, md, vd = (to_dev(x) for x in (p, g, m, v))
+    lr, b1, b2, eps = 0.01, 0.9, 0.999, 1e-8
+    pr, mr, vr = p.astype(np.float64), m.astype(np.float64), v.astype(np.float64)
+    for step in (1, 2, 3):
+        ops.adam_step(pd, gd, md, vd, lr / (1 - b1 ** step), 1 / np.sqrt(1 - b2 ** step), b1, b2, eps)
+        pr, mr, vr = orc.adam_step(pr, g.astype(np.float64), mr, vr, step, lr, b1, b2, eps)
+    np.testing.assert_allclose(pd.cpu().numpy(), pr, rtol=1e-5, atol=1e-6)
+
+
+def test_bounded_wait_reports_timeout_and_context_survives():
+    flag = torch.zeros(1, dtype=torch.int32, device="cuda")
+    ops.wait_flag(flag, 50_000_000)  # 50 ms, nobody sets the flag
+    assert _native.read_device_error(0) == 7
+    x = torch.ones(4, device="cuda")
+    assert float((x * 2).sum().item()) == 8.0
