@@ -158,7 +158,7 @@ def test_eval_terms(prec, golden):
     ref = orc.eval_terms(g["A"], g["B"], idx, g["S_value"])
     np.testing.assert_allclose(out, ref, rtol=TOL[prec] * 10, atol=1e-9)
     np.testing.assert_allclose(orc.metrics_from_terms(out), [g["rmse"], g["jacc"], g["cost"]],
-                               rtol=1e-4)
+                               rtol=1e-4 if prec == ops.SUMAC_3XTF32 else 2e-3)
 
 
 def test_adam_matches_oracle():
