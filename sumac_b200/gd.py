@@ -1,0 +1,176 @@
+"""GD solver (src/sumac/training/gd.py:110-253) driving the native block gradient and optimizer.
+
+Per batch of row blocks: the loss terms (report epochs only, before the step, as the reference
+computes its loss in the forward pass), the block gradients ``sumac_gd_block_grad`` (two fused
+tcgen05 passes, no b x n intermediate), then one optimizer step over both full factors
+(Adam/AdamW/SGD natively; Muon through torch.optim.Muon on the unpadded views).
+"""
+from __future__ import annotations
+
+import math
+import time
+
+import torch
+from torch import Tensor
+from torch.utils.data import DataLoader
+
+from . import _native, ops
+from .config import OptimizerName, SumacConfig
+from .data import SparseDirection
+from .metrics import Evaluator, metrics_from_terms
+from .salsa import draw_perm, init_salsa_factors
+
+
+class _Optimizer:
+    """torch.optim semantics over the padded factors (training/gd.py:20-46)."""
+
+    def __init__(self, cfg: SumacConfig, params: list[Tensor], grads: list[Tensor], d: int):
+        self.cfg = cfg
+        self.params = params
+        self.grads = grads
+        self.kind = cfg.optimizer
+        self.step_count = 0
+        if self.kind in (OptimizerName.ADAM, OptimizerName.ADAMW):
+            self.m = [torch.zeros_like(p) for p in params]
+            self.v = [torch.zeros_like(p) for p in params]
+        elif self.kind == OptimizerName.SGD:
+            self.buf = [torch.zeros_like(p) for p in params]
+            self.sumsq = torch.zeros(1, dtype=torch.float64, device=params[0].device)
+        elif self.kind == OptimizerName.MUON:
+            self.views = [torch.nn.Parameter(p[:, :d]) for p in params]
+            self.torch_opt = torch.optim.Muon(self.views, lr=cfg.learning_rate, weight_decay=0.0,
+                                              momentum=cfg.momentum,
+                                              adjust_lr_fn="match_rms_adamw")
+        else:
+            raise ValueError(f"Unknown optimizer: {cfg.optimizer}")
+
+    def step(self) -> None:
+        self.step_count += 1
+        t = self.step_count
+        cfg = self.cfg
+        if self.kind in (OptimizerName.ADAM, OptimizerName.ADAMW):
+            b1, b2 = cfg.adam_betas
+            lr_bc1 = cfg.learning_rate / (1.0 - b1 ** t)
+            inv_sqrt_bc2 = 1.0 / math.sqrt(1.0 - b2 ** t)
+            for p, g, m, v in zip(self.params, self.grads, self.m, self.v):
+                ops.adam_step(p, g, m, v, lr_bc1, inv_sqrt_bc2, b1, b2, cfg.adam_eps)
+        elif self.kind == OptimizerName.SGD:
+            # clip_grad_norm_([A, B], max_norm=1.0) then SGD with momentum (gd.py:43-46)
+            self.sumsq.zero_()
+            for g in self.grads:
+                ops.grad_sumsq(g, self.sumsq)
+            for p, g, buf in zip(self.params, self.grads, self.buf):
+                ops.sgd_step(p, g, buf, cfg.learning_rate, cfg.momentum, t == 1, self.sumsq, 1.0)
+        else:
+            with torch.no_grad():
+                for view, g in zip(self.views, self.grads):
+                    view.grad = g[:, :view.shape[1]]
+                self.torch_opt.step()
+
+
+def _rows_csr(S_index, S_value, perm, m):
+    """Support by global position in ``perm`` (local row of a block = position - k*bs):
+    rowptr[m+1] over positions, entries {column, value bits}. Built once (GD keeps its
+    partition for the whole run, gd.py:134-150)."""
+    dev = S_value.device
+    perm_inv = torch.empty_like(perm)
+    perm_inv[perm] = torch.arange(m, device=dev)
+    pos = perm_inv[S_index[0]]
+    order = torch.sort(pos, stable=True).indices
+    pos_sorted = pos[order]
+    rowptr = torch.searchsorted(pos_sorted, torch.arange(m + 1, device=dev)).to(torch.int32)
+    ent = torch.stack([S_index[1][order].to(torch.int32),
+                       S_value[order].to(torch.float32).view(torch.int32)], dim=1).contiguous()
+    return rowptr, ent
+
+
+def GD_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfig,
+            A_init: Tensor | None = None, B_init: Tensor | None = None):
+    assert cfg.num_blocks is not None and cfg.device is not None
+    dev = cfg.device
+    gen, gen_blocks, gen_loader = cfg.get_generator()
+    S_index = S_index.to(dev)
+    S_value = S_value.to(dev)
+    d = cfg.rank
+    if A_init is None or B_init is None:
+        A, B = init_salsa_factors(S_index, S_value, m, n, d, gen)
+    else:
+        A, B = A_init.to(dev).clone(), B_init.to(dev).clone()
+    Dp = ops.padded_rank(d)
+    prec = cfg.precision()
+    Ap = ops.pad_factor(A.detach().to(torch.float32), Dp)
+    Bp = ops.pad_factor(B.detach().to(torch.float32), Dp)
+    gA = torch.zeros_like(Ap)
+    gB = torch.zeros_like(Bp)
+    opt = _Optimizer(cfg, [Ap, Bp], [gA, gB], d)
+
+    nb = cfg.num_blocks
+    perm = draw_perm(m, gen_blocks, dev)       # one partition for the whole run (datasets.py:34)
+    bs = (m + nb - 1) // nb
+    dir_b = SparseDirection(S_index[0], S_index[1], S_value, m, n, nb)
+    dir_b.rebuild(perm)                        # by column j, entries {local row, S}
+    rowptr_pos, ent_pos = _rows_csr(S_index, S_value, perm, m)
+    blocks = []
+    for k in range(nb):
+        rows = perm[k * bs:min(m, (k + 1) * bs)]
+        blocks.append((rows, dir_b.block_rowptr(k), rowptr_pos[k * bs:k * bs + rows.numel() + 1]))
+    loader = DataLoader(list(range(nb)), batch_size=cfg.batch_blocks, shuffle=cfg.shuffle_blocks,
+                        collate_fn=lambda b: b, generator=gen_loader)
+    evaluator = Evaluator(S_index, S_value, d, prec)
+    sum_v = float(S_value.double().sum().item())
+    s_norm = float(torch.linalg.norm(S_value.double()).item())
+
+    rmse, jacc, errZ = evaluator(Ap, Bp)
+    if cfg.verbose:
+        print(f"[epoch 0/{cfg.max_iterations}]: cost = {errZ:.6f}, rmse = {rmse:.6f}, "
+              f"jacc = {jacc:.6f}, time = 0.0000s")
+    hist = {"cost": [], "rmse": [], "jacc": [], "time": []}
+    terms = torch.zeros(8, dtype=torch.float64, device=dev)
+    t0 = time.time()
+    for epoch in range(1, cfg.max_iterations + 1):
+        report = epoch % cfg.eval_interval == 0
+        if report:
+            terms.zero_()
+        for batch in loader:
+            for i, k in enumerate(batch):
+                rows, rp_b, rp_a = blocks[k]
+                if rows.numel() == 0:
+                    continue
+                if report:
+                    ops.block_loss_terms(Ap, Bp, d, rows, rp_b, dir_b.ent, terms, 1, prec)
+            ops.fill_zero(gA)
+            first = True
+            for k in batch:
+                rows, rp_b, rp_a = blocks[k]
+                if rows.numel() == 0:
+                    continue
+                ops.gd_block_grad(Ap, Bp, d, rows, rp_b, dir_b.ent, rp_a, ent_pos, gA, gB,
+                                  0 if first else 1, prec)
+                first = False
+            if first:
+                ops.fill_zero(gB)
+            opt.step()
+        if report:
+            t = terms.cpu().tolist()
+            sum_sr, sum_sr2, obs_sq, res_m, res_l, jnum = t[:6]
+            total_errz = sum_sr2 - obs_sq + res_l
+            total_mse = sum_sr2 - obs_sq + res_m
+            jacc = 1.0 - jnum / (sum_v + sum_sr - jnum)
+            rmse = math.sqrt(max(total_mse, 0.0)) / (s_norm + 1e-16)
+            errZ = math.sqrt(max(total_errz, 0.0)) / (s_norm + 1e-16)
+            elapsed = time.time() - t0
+            hist["cost"].append(errZ)
+            hist["rmse"].append(rmse)
+            hist["jacc"].append(jacc)
+            hist["time"].append(elapsed)
+            if cfg.verbose:
+                print(f"[epoch {epoch}/{cfg.max_iterations}]: cost = {errZ:.6f}, "
+                      f"rmse = {rmse:.6f}, jacc = {jacc:.6f}, time = {elapsed:.4f}s")
+    _native.raise_device_error(dev)
+    total = time.time() - t0
+    if cfg.verbose:
+        print(f"\nTotal elapsed time: {total:.2f} sec")
+    rmse, jacc, errZ = evaluator(Ap, Bp)
+    if cfg.verbose:
+        print(f"EVAL: cost={errZ:.6f}, rmse={rmse:.6f}, jacc={jacc:.6f}, time={total:.4f}s")
+    return Ap[:, :d].contiguous(), Bp[:, :d].contiguous(), hist

@@ -1,0 +1,158 @@
+"""SALSA solver (src/sumac/training/salsa.py:212-355) driving the native block update.
+
+Per iteration: two reshuffles (one row permutation per factor, drawn from the same seeded
+generators as the reference), a device-side rebuild of the per-block CSR of both directions, then
+for every block k the update of B against A's row block k followed by the update of A against B's
+row block k. Each block update is one ``sumac_salsa_block_update`` call (gather + Gram + LU solve,
+the fused tcgen05 product, and the finalize pass with the sparse correction and momentum step).
+"""
+from __future__ import annotations
+
+import time
+
+import numpy as np
+import torch
+from torch import Tensor
+
+from . import _native, ops
+from .config import SumacConfig
+from .data import SparseDirection
+from .metrics import Evaluator
+
+
+def refactor(A: Tensor, B: Tensor) -> tuple[Tensor, Tensor]:
+    """A B^T unchanged, singular values shared (training/salsa.py:20-33)."""
+    Qa, Ra = torch.linalg.qr(A, mode="reduced")
+    Qb, Rb = torch.linalg.qr(B, mode="reduced")
+    U, S, Vh = torch.linalg.svd(Ra @ Rb.T, full_matrices=False)
+    sqrtS = torch.diag(torch.sqrt(S))
+    return Qa @ U @ sqrtS, Qb @ Vh.T @ sqrtS
+
+
+def init_salsa_factors(S_index, S_value, m, n, d, gen):
+    """A > 0, B < 0 from S times uniform noise, rescaled, then refactored
+    (training/salsa.py:36-78); draws from `gen` in the same order as the reference."""
+    device, dtype = S_value.device, S_value.dtype
+    with torch.sparse.check_sparse_tensor_invariants(False):
+        S = torch.sparse_coo_tensor(S_index.to(device=device, dtype=torch.long), S_value,
+                                    size=(m, n), device=device, dtype=dtype).coalesce()
+        R_A = torch.rand((n, d), device=device, dtype=dtype, generator=gen)
+        R_B = torch.rand((m, d), device=device, dtype=dtype, generator=gen)
+        A = torch.sqrt(torch.sparse.mm(S, R_A))
+        B = -torch.sqrt(torch.sparse.mm(S.T, R_B))
+    Lij = torch.sum(A[S_index[0], :] * B[S_index[1], :], dim=1)
+    ssqS = torch.sum(S_value ** 2)
+    ssqL = torch.sum(Lij ** 2)
+    SdotL = torch.sum(S_value * Lij)
+    a, b, c = ssqL, -2.0 * SdotL, -3.0 * ssqS
+    alpha = (-b + torch.sqrt(b ** 2 - 4 * a * c)) / (2 * a)
+    scale = torch.clamp(torch.sqrt(alpha), 0.0, 1.0)
+    return refactor(scale * A, scale * B)
+
+
+def draw_perm(m: int, gen: torch.Generator, device) -> Tensor:
+    """torch.randperm on the generator's device (datasets.py:39), moved to the training device."""
+    return torch.randperm(m, device=gen.device, generator=gen).to(device)
+
+
+def unbias_values(momentum: float, first_step: int, count: int) -> np.ndarray:
+    """1 - momentum^step in float32 for steps first_step .. first_step+count-1 (salsa.py:302-303)."""
+    mu = np.float32(momentum)
+    return np.array([np.float32(1.0) - mu ** np.float32(s)
+                     for s in range(first_step, first_step + count)], dtype=np.float32)
+
+
+class SalsaState:
+    """Device state of one SALSA run: padded factors, momentum, both directions' CSR."""
+
+    def __init__(self, S_index, S_value, m, n, cfg: SumacConfig, A, B):
+        dev = cfg.device
+        self.d = cfg.rank
+        self.Dp = ops.padded_rank(self.d)
+        self.m, self.n = m, n
+        self.nb = cfg.num_blocks
+        self.prec = cfg.precision()
+        self.Ap = ops.pad_factor(A.to(torch.float32), self.Dp)
+        self.Bp = ops.pad_factor(B.to(torch.float32), self.Dp)
+        self.dA = torch.zeros_like(self.Ap)
+        self.dB = torch.zeros_like(self.Bp)
+        # B-update: fixed = rows of A (S rows), updated rows = columns of S
+        self.dir_b = SparseDirection(S_index[0], S_index[1], S_value, m, n, self.nb)
+        # A-update: fixed = rows of B (S columns), updated rows = rows of S
+        self.dir_a = SparseDirection(S_index[1], S_index[0], S_value, n, m, self.nb)
+        self.momentum = float(cfg.momentum)
+        self.lrate = float(np.float32(cfg.learning_rate))
+        self.unbias = torch.empty(self.nb, dtype=torch.float32, device=dev)
+        self.unbias_host = torch.empty(self.nb, dtype=torch.float32).pin_memory() \
+            if torch.cuda.is_available() else None
+        L = _native.lib()
+        self.ws_b = ops._ws(dev, L.sumac_salsa_update_workspace_bytes(
+            n, self.dir_b.block_size, self.d, self.prec), "salsa_b")
+        self.ws_a = ops._ws(dev, L.sumac_salsa_update_workspace_bytes(
+            m, self.dir_a.block_size, self.d, self.prec), "salsa_a")
+
+    def iteration(self, it: int, perm_r: Tensor, perm_c: Tensor) -> None:
+        nb = self.nb
+        self.dir_b.rebuild(perm_r)
+        self.dir_a.rebuild(perm_c)
+        self.unbias_host.copy_(torch.from_numpy(unbias_values(self.momentum, 1 + (it - 1) * nb, nb)))
+        self.unbias.copy_(self.unbias_host, non_blocking=True)
+        for k in range(nb):
+            rows = self.dir_b.block_rows(perm_r, k)
+            if rows.numel() > 0:
+                ops.salsa_block_update(self.Ap, rows, self.Bp, self.dB, self.d,
+                                       self.dir_b.block_rowptr(k), self.dir_b.ent, self.momentum,
+                                       self.lrate, self.unbias[k:k + 1], self.prec, self.ws_b)
+            rows = self.dir_a.block_rows(perm_c, k)
+            if rows.numel() > 0:
+                ops.salsa_block_update(self.Bp, rows, self.Ap, self.dA, self.d,
+                                       self.dir_a.block_rowptr(k), self.dir_a.ent, self.momentum,
+                                       self.lrate, self.unbias[k:k + 1], self.prec, self.ws_a)
+
+    def factors(self):
+        return (self.Ap[:, :self.d].contiguous(), self.Bp[:, :self.d].contiguous())
+
+
+def salsa_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfig,
+               A_init: Tensor | None = None, B_init: Tensor | None = None):
+    """Same schedule, generators and history as the reference's salsa_loop."""
+    assert cfg.num_blocks is not None and cfg.device is not None
+    gen, gen_rows, gen_cols = cfg.get_generator()
+    dev = cfg.device
+    S_index = S_index.to(dev)
+    S_value = S_value.to(dev)
+    if A_init is None or B_init is None:
+        A, B = init_salsa_factors(S_index, S_value, m, n, cfg.rank, gen)
+    else:
+        A, B = A_init.to(dev), B_init.to(dev)
+    st = SalsaState(S_index, S_value, m, n, cfg, A, B)
+    evaluator = Evaluator(S_index, S_value, cfg.rank, st.prec)
+    # the reference's datasets draw one permutation each at construction (datasets.py:34)
+    draw_perm(m, gen_rows, dev)
+    draw_perm(n, gen_cols, dev)
+    rmse, jacc, errZ = evaluator(st.Ap, st.Bp)
+    if cfg.verbose:
+        print(f"[epoch 0/{cfg.max_iterations}]: cost = {errZ:.6f}, rmse = {rmse:.6f}, "
+              f"jacc = {jacc:.6f}, time = 0.0000s")
+    hist = {"cost": [], "rmse": [], "jacc": [], "time": []}
+    t0 = time.time()
+    for it in range(1, cfg.max_iterations + 1):
+        perm_r = draw_perm(m, gen_rows, dev)
+        perm_c = draw_perm(n, gen_cols, dev)
+        st.iteration(it, perm_r, perm_c)
+        if cfg.eval_interval is not None and it % cfg.eval_interval == 0:
+            rmse, jacc, errZ = evaluator(st.Ap, st.Bp)
+            _native.raise_device_error(dev)
+            elapsed = time.time() - t0
+            hist["cost"].append(errZ)
+            hist["rmse"].append(rmse)
+            hist["jacc"].append(jacc)
+            hist["time"].append(elapsed)
+            if cfg.verbose:
+                print(f"[epoch {it}/{cfg.max_iterations}]: cost = {errZ:.6f}, rmse = {rmse:.6f}, "
+                      f"jacc = {jacc:.6f}, time = {elapsed:.4f}s")
+    _native.raise_device_error(dev)
+    if cfg.verbose:
+        print(f"\nTotal elapsed time: {time.time() - t0:.2f} sec")
+    A, B = st.factors()
+    return A, B, hist

@@ -1,0 +1,95 @@
+"""End-to-end parity of sumac_factorize on the GPU with runs of the reference on the CPU
+(tests/golden/e2e_*.npz), with the permutations drawn on the CPU (perm_device="cpu") so both runs
+see the same row blocks; plus the reference's planted low-rank convergence check
+(tests/test_sumac.py:75-126 of the reference)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+import torch.nn.functional as F
+
+from sumac_b200 import OptimizerName, SumacConfig, SumacMethod, sumac_factorize
+from tests.helpers import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _run(g, method, **extra):
+    cfg = SumacConfig(method=method, rank=int(g["rank"]), max_iterations=int(g["iters"]),
+                      num_blocks=int(g["num_blocks"]), seed=int(g["seed"]),
+                      learning_rate=float(g["lr"]), verbose=False, perm_device="cpu", **extra)
+    return sumac_factorize(S_index=torch.from_numpy(g["S_index"]).cuda(),
+                           S_value=torch.from_numpy(g["S_value"]).cuda(),
+                           shape=(int(g["m"]), int(g["n"])),
+                           A_init=torch.from_numpy(g["A0"]).cuda(),
+                           B_init=torch.from_numpy(g["B0"]).cuda(), config=cfg)
+
+
+def test_salsa_matches_reference_run(golden):
+    g = golden("e2e_salsa")
+    A, B, hist = _run(g, SumacMethod.SALSA, eval_interval=1)
+    assert rel_err(A.cpu().numpy(), g["A"]) < 1e-4
+    assert rel_err(B.cpu().numpy(), g["B"]) < 1e-4
+    for key in ("cost", "rmse", "jacc"):
+        np.testing.assert_allclose(hist[key], g[key], rtol=1e-4)
+
+
+def test_salsa_tf32_mode_close_to_reference(golden):
+    g = golden("e2e_salsa")
+    A, B, hist = _run(g, SumacMethod.SALSA, eval_interval=1, allow_tf32=True)
+    np.testing.assert_allclose(hist["cost"], g["cost"], rtol=1e-2)
+
+
+def test_gd_matches_reference_run(golden):
+    g = golden("e2e_gd")
+    A, B, hist = _run(g, SumacMethod.GD, eval_interval=2, batch_blocks=int(g["batch_blocks"]),
+                      shuffle_blocks=True)
+    assert rel_err(A.cpu().numpy(), g["A"]) < 1e-4
+    assert rel_err(B.cpu().numpy(), g["B"]) < 1e-4
+    for key in ("cost", "rmse", "jacc"):
+        np.testing.assert_allclose(hist[key], g[key], rtol=1e-4)
+
+
+def test_returns_on_requested_device_and_leaves_inputs(golden):
+    g = golden("e2e_salsa")
+    S_index = torch.from_numpy(g["S_index"])
+    S_value = torch.from_numpy(g["S_value"])
+    before = (S_index.clone(), S_value.clone())
+    prec = torch.get_float32_matmul_precision()
+    cfg = SumacConfig(rank=4, max_iterations=1, num_blocks=2, seed=0, verbose=False)
+    A, B, _ = sumac_factorize(S_index=S_index, S_value=S_value, shape=(int(g["m"]), int(g["n"])),
+                              config=cfg)
+    assert A.device.type == "cpu" and A.shape == (int(g["m"]), 4)
+    assert torch.equal(S_index, before[0]) and torch.equal(S_value, before[1])
+    assert torch.get_float32_matmul_precision() == prec
+
+
+def _low_rank(m, n, d, density, seed=0):
+    torch.manual_seed(seed)
+    A = torch.randn(m, d)
+    B = torch.randn(n, d)
+    L = A @ B.T
+    flat = L.flatten()
+    bias = torch.sort(flat, descending=True)[0][math.ceil(len(flat) * density)]
+    S = torch.relu(L - bias)
+    sp = S.to_sparse()
+    return sp.indices(), sp.values().float(), S
+
+
+@pytest.mark.parametrize("method,num_blocks", [(SumacMethod.GD, 2), (SumacMethod.SALSA, 25)])
+def test_low_rank_convergence(method, num_blocks):
+    idx, val, S = _low_rank(10000, 10000, 16, 0.01)
+    cfg = SumacConfig(rank=16, max_iterations=300, method=method, learning_rate=0.1,
+                      num_blocks=num_blocks, seed=0, verbose=False)
+    A, B, _ = sumac_factorize(S_index=idx.cuda(), S_value=val.cuda(), shape=(10000, 10000),
+                              config=cfg)
+    mse = F.mse_loss(torch.relu(A @ B.T), S.cuda()).item()
+    assert mse < 0.08, mse
+
+
+@pytest.mark.parametrize("opt", [OptimizerName.SGD, OptimizerName.ADAMW])
+def test_gd_other_optimizers_run(golden, opt):
+    g = golden("e2e_gd")
+    A, B, hist = _run(g, SumacMethod.GD, eval_interval=2, batch_blocks=2, optimizer=opt)
+    assert np.isfinite(A.cpu().numpy()).all() and len(hist["cost"]) == 2
