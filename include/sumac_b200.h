@@ -44,6 +44,20 @@ int sumac_padded_rank(int d);
 const char* sumac_last_error(void);
 /* Time limit for device-side waits (nanoseconds, default 2e9). */
 void sumac_set_timeout_ns(unsigned long long ns);
+/* Number of kernels this library has launched since it was loaded (all threads and devices). */
+long long sumac_kernel_launches(void);
+
+/*
+ * The fused product alone on prepared operands (the benchmark view of the hot kernel, as the
+ * reference's kernel_benchmarks/relu_bat_c_bench.py times relu_bat_c alone):
+ * partials[s][M][Dp] = sum over the chunks of split s of ReLU(X F^T) C, with X[M][Dp],
+ * F{hi,lo}[N][Dp], Ct{hi,lo}[Dp][ldct] = C^T (tf32 hi / lo split for SUMAC_3XTF32; lo may be NULL
+ * for SUMAC_TF32). The number of splits s is sumac_relu_product_splits(M, N, Dp, precision).
+ */
+int sumac_relu_product_splits(int64_t M, int64_t N, int Dp, int precision);
+int sumac_relu_product(const float* X, int64_t M, const float* Fhi, const float* Flo,
+                       const float* Cthi, const float* Ctlo, int64_t ldct, int64_t N, int Dp,
+                       int precision, float* partials, int* dev_err, sumac_stream_t stream);
 
 /*
  * relu_bat_c: Y[M][D] = ReLU(B[M][D] A[N][D]^T) C[N][D], plain (unpadded) row-major inputs.

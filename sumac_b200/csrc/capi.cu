@@ -88,6 +88,24 @@ extern "C" {
 int sumac_version(void) { return 1; }
 const char* sumac_last_error(void) { return g_last_error.c_str(); }
 int sumac_padded_rank(int d) { return padded(d); }
+long long sumac_kernel_launches(void) { return launch_count(); }
+
+int sumac_relu_product(const float* X, int64_t M, const float* Fhi, const float* Flo,
+                       const float* Cthi, const float* Ctlo, int64_t ldct, int64_t N, int Dp,
+                       int precision, float* partials, int* dev_err, sumac_stream_t stream) {
+  const bool x3 = precision == SUMAC_3XTF32;
+  if (!X || !Fhi || !Cthi || !partials || !dev_err || (x3 && (!Flo || !Ctlo)))
+    return fail(SUMAC_ERR_ARG, "relu_product: null pointer");
+  if (!aligned16(X) || !aligned16(Fhi) || !aligned16(Cthi) || (ldct & 3))
+    return fail(SUMAC_ERR_ARG, "relu_product: operands must be 16-byte aligned");
+  int rc = launch_relu_product(X, M, Fhi, Flo, Cthi, Ctlo, ldct, N, Dp, x3, partials, dev_err,
+                               num_sms_current(), g_timeout_ns,
+                               reinterpret_cast<cudaStream_t>(stream));
+  return cuda_status(rc, "relu_product");
+}
+int sumac_relu_product_splits(int64_t M, int64_t N, int Dp, int precision) {
+  return product_split_count(M, N, Dp, precision == SUMAC_3XTF32, num_sms_current());
+}
 void sumac_set_timeout_ns(unsigned long long ns) { g_timeout_ns = ns; }
 int sumac_num_sms(int device) {
   int n = 0;

@@ -1,12 +1,17 @@
 // kernels.cu — HBM / latency-bound kernels around the fused product: packing, the SALSA
 // Gram + solve, the finalize pass (sparse correction + momentum update or gradient store), the
 // deterministic per-block CSR builder, loss / metric terms and the optimizer steps.
+#include <atomic>
 #include <cstdint>
 
 #include "kernels.cuh"
 #include "sm100.cuh"
 
 namespace sb {
+
+static std::atomic<long long> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
 static inline int cdiv64(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
 static inline unsigned grid_cap(int64_t work, int threads, int64_t cap) {
@@ -43,6 +48,7 @@ void launch_gather_pad(const float* src, int64_t ld_src, int d, const int64_t* r
                        int Dp, float* dst, float* dst_hi, float* dst_lo, cudaStream_t stream) {
   const int64_t total = nrows * Dp;
   if (total == 0) return;
+  count_launch();
   gather_pad_kernel<<<grid_cap(total, 256, 148 * 16), 256, 0, stream>>>(src, ld_src, d, rows,
                                                                          nrows, Dp, dst, dst_hi,
                                                                          dst_lo);
@@ -81,6 +87,7 @@ void launch_transpose_split(const float* src, int64_t nrows, int Dp, float* dst_
                             int64_t ld_dst, cudaStream_t stream) {
   if (nrows == 0) return;
   dim3 grid((unsigned)((nrows + 31) / 32), (unsigned)((Dp + 31) / 32));
+  count_launch();
   transpose_split_kernel<<<grid, dim3(32, 8), 0, stream>>>(src, nrows, Dp, dst_hi, dst_lo, ld_dst);
 }
 
@@ -134,6 +141,7 @@ __global__ void gram_kernel(const float* __restrict__ FI, int64_t b, int d, int 
 
 void launch_gram(const float* FI, int64_t b, int d, int Dp, double* gram_ws, cudaStream_t stream) {
   dim3 grid(gram_parts(b), (d * d + 2047) / 2048);
+  count_launch();
   gram_kernel<<<grid, 256, 64 * d * sizeof(float), stream>>>(FI, b, d, Dp, gram_ws);
 }
 
@@ -231,6 +239,7 @@ void launch_solve(const float* FI, int64_t b, int d, int Dp, const double* gram_
   const size_t smem = (size_t)d * d * sizeof(double) + (size_t)d * sizeof(int) + 16;
   if (smem > 48 * 1024)
     cudaFuncSetAttribute(solve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  count_launch();
   solve_kernel<<<grid, 128, smem, stream>>>(FI, b, d, Dp, gram_ws, nparts, P, Cthi, Ctlo, ldct, err);
 }
 
@@ -361,6 +370,7 @@ void launch_finalize(const FinalizeArgs& a, cudaStream_t stream) {
   const int threads = 256;
   const int G = a.Dp / 4 < 32 ? a.Dp / 4 : 32;
   const unsigned grid = grid_cap(a.M * G, threads, 148 * 8);
+  count_launch();
   switch (a.Dp) {
     case 16: finalize_kernel<16><<<grid, threads, 0, stream>>>(a); break;
     case 32: finalize_kernel<32><<<grid, threads, 0, stream>>>(a); break;
@@ -566,20 +576,26 @@ int launch_block_csr(const int64_t* perm, int64_t m_fixed, int num_blocks, const
   int* ntask = reinterpret_cast<int*>(w + L.off_ntask);
   int4* tasks = reinterpret_cast<int4*>(w + L.off_tasks);
   const int bs = (int)((m_fixed + num_blocks - 1) / num_blocks);
+  count_launch();
   perm_inv_kernel<<<grid_cap(m_fixed, 256, 148 * 8), 256, 0, stream>>>(perm, m_fixed, inv, ntask);
   if (nnz > 0) {
+    count_launch();
     csr_hist_kernel<<<L.ncta, CSR_THREADS, num_blocks * sizeof(int), stream>>>(
         e_fixed, nnz, L.chunk, inv, bs, num_blocks, hist);
+    count_launch();
     scan_exclusive_kernel<<<1, 1024, 0, stream>>>(hist, (int64_t)num_blocks * L.ncta);
     const size_t smem = (size_t)9 * num_blocks * sizeof(int);
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(csr_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    count_launch();
     csr_scatter_kernel<<<L.ncta, CSR_THREADS, smem, stream>>>(e_fixed, e_out, e_val, nnz, L.chunk,
                                                              inv, bs, num_blocks, M, hist, keys, ent);
   }
   const int64_t nkeys = (int64_t)num_blocks * M;
+  count_launch();
   csr_rowptr_kernel<<<grid_cap(nnz > 0 ? nnz : 1, 256, INT32_MAX), 256, 0, stream>>>(
       keys, nnz, nkeys, rowptr, ntask, tasks, L.max_tasks);
+  count_launch();
   csr_fill_tasks_kernel<<<148 * 2, 256, 0, stream>>>(ntask, tasks, L.max_tasks, rowptr);
   return (int)cudaGetLastError();
 }
@@ -640,6 +656,7 @@ __global__ void sparse_terms_coo_kernel(const float* __restrict__ A, const float
 void launch_sparse_terms_coo(const float* A, const float* B, int Dp, const int32_t* ei,
                              const int32_t* ej, const float* v, int64_t nnz, double* partials,
                              int grid, cudaStream_t stream) {
+  count_launch();
   sparse_terms_coo_kernel<<<grid, 256, 0, stream>>>(A, B, Dp, ei, ej, v, nnz, partials);
 }
 
@@ -667,6 +684,7 @@ __global__ void sparse_terms_csr_kernel(const float* __restrict__ X, const float
 void launch_sparse_terms_csr(const float* X, const float* F, int Dp, const int32_t* rowptr,
                              int64_t M, const int2* ent, double* partials, int grid,
                              cudaStream_t stream) {
+  count_launch();
   sparse_terms_csr_kernel<<<grid, 256, 0, stream>>>(X, F, Dp, rowptr, M, ent, partials);
 }
 
@@ -681,6 +699,7 @@ __global__ void sum_partials_kernel(const double* __restrict__ partials, int n, 
 
 void launch_sum_partials(const double* partials, int n, int w, double* out, int accumulate,
                          cudaStream_t stream) {
+  count_launch();
   sum_partials_kernel<<<1, 32, 0, stream>>>(partials, n, w, out, accumulate);
 }
 
@@ -708,6 +727,7 @@ __global__ void adam_kernel(float* __restrict__ p, const float* __restrict__ g, 
 void launch_adam(float* p, const float* g, float* m, float* v, int64_t n, float lr_over_bc1,
                  float inv_sqrt_bc2, float beta1, float beta2, float eps, cudaStream_t stream) {
   if (n == 0) return;
+  count_launch();
   adam_kernel<<<grid_cap(n, 256, 148 * 16), 256, 0, stream>>>(p, g, m, v, n, lr_over_bc1,
                                                                inv_sqrt_bc2, beta1, beta2, eps);
 }
@@ -720,6 +740,7 @@ __global__ void fill_zero_kernel(float* __restrict__ p, int64_t n) {
 
 void launch_fill_zero(float* p, int64_t n, cudaStream_t stream) {
   if (n == 0) return;
+  count_launch();
   fill_zero_kernel<<<grid_cap(n, 256, 148 * 16), 256, 0, stream>>>(p, n);
 }
 
@@ -735,6 +756,7 @@ __global__ void sumsq_kernel(const float* __restrict__ g, int64_t n, double* out
 
 void launch_sumsq(const float* g, int64_t n, double* out, cudaStream_t stream) {
   if (n == 0) return;
+  count_launch();
   sumsq_kernel<<<grid_cap(n, 256, 148 * 4), 256, 0, stream>>>(g, n, out);
 }
 
@@ -763,6 +785,7 @@ __global__ void sgd_kernel(float* __restrict__ p, float* __restrict__ g, float* 
 void launch_sgd(float* p, float* g, float* buf, int64_t n, float lr, float momentum, int first,
                 const double* sumsq, float max_norm, cudaStream_t stream) {
   if (n == 0) return;
+  count_launch();
   sgd_kernel<<<grid_cap(n, 256, 148 * 16), 256, 0, stream>>>(p, g, buf, n, lr, momentum, first,
                                                               sumsq, max_norm);
 }
@@ -781,6 +804,7 @@ __global__ void wait_flag_kernel(const volatile int* flag, int* err, unsigned lo
 }
 
 void launch_wait_flag(const int* flag, int* err, unsigned long long timeout_ns, cudaStream_t s) {
+  count_launch();
   wait_flag_kernel<<<1, 1, 0, s>>>(flag, err, timeout_ns);
 }
 

@@ -7,6 +7,10 @@
 
 namespace sb {
 
+// Number of kernels this library has launched (all threads, all devices).
+void count_launch();
+long long launch_count();
+
 // ---- fused product / reduce (product.cu) ---------------------------------------------------
 // X [M][Dp], F{hi,lo} [N][Dp], Ct{hi,lo} [Dp][ldct] (row-major, 16-byte aligned rows).
 // Writes ws[splits][M][Dp] partial products (splits = product_split_count(...)). Returns 0 or a

@@ -123,6 +123,7 @@ static int run_kernel(const CUtensorMap& mx, const CUtensorMap& mfh, const CUten
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
   if (e != cudaSuccess) return (int)e;
+  count_launch();
   kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(mx, mfh, mfl, mch, mcl, p);
   return (int)cudaGetLastError();
 }
