@@ -1,0 +1,431 @@
+"""Benchmark of sumac_b200 on BASELINE.json's metric.
+
+Workload (default): config C4, the graph-shaped square matrix m = n = 139255 with 19,773,733
+nonzeros (log-normal degrees, endpoints proportional to degree, values log(1+k), k geometric),
+factorised by SALSA with rank 16 and 100 blocks. The data are seeded synthetic stand-ins for the
+connectome matrix (the real dataset is not available here).
+
+One step = one SALSA iteration (two reshuffles, CSR rebuilds and 2 x 100 block updates) with the
+data already resident on the GPU. `value` = iterations/s of the whole job (max over ranks).
+`e2e` = the same metric through sumac_factorize() with the inputs in host memory (copies, pruning,
+initialisation and validation included). The fused tcgen05 product of one block update is also
+timed alone with CUDA events for the roofline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c4|c3|c2]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+CONFIGS = {
+    # name: (generator, rank, num_blocks, description)
+    "c4": dict(rank=16, num_blocks=100, desc="C4 graph-shaped 139255x139255, nnz 19773733, SALSA rank 16, 100 blocks"),
+    "c3": dict(rank=64, num_blocks=50, desc="C3 bigram-shaped 50000x50000, nnz~10M, SALSA rank 64, 50 blocks"),
+    "c2": dict(rank=32, num_blocks=20, desc="C2 digits-shaped 70000x784, density 0.19, SALSA rank 32, 20 blocks"),
+}
+
+
+# ------------------------------------------------------------------------------ synthetic data
+def _sample_pairs(rng, p_row, p_col, n_cols, target):
+    """Distinct (row, col) pairs drawn with probability p_row[r] p_col[c] (inverse-CDF sampling,
+    duplicates merged, topped up until `target` distinct pairs, then a uniform subset). The
+    uniforms come from the seeded numpy generator; the integer work runs in torch (on the GPU when
+    there is one), so the result does not depend on where it runs."""
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    cr = torch.from_numpy(np.cumsum(p_row)).to(dev)
+    cc = torch.from_numpy(np.cumsum(p_col)).to(dev)
+    cr /= cr[-1].clone()
+    cc /= cc[-1].clone()
+    keys = torch.empty(0, dtype=torch.int64, device=dev)
+    while keys.numel() < target:
+        need = int((target - keys.numel()) * 1.3) + 10000
+        u = torch.from_numpy(rng.random(need)).to(dev)
+        r = torch.clamp(torch.searchsorted(cr, u), max=p_row.size - 1)
+        u = torch.from_numpy(rng.random(need)).to(dev)
+        c = torch.clamp(torch.searchsorted(cc, u), max=p_col.size - 1)
+        keys = torch.unique(torch.cat([keys, r * n_cols + c]))
+    keys = keys.cpu().numpy()
+    if keys.size > target:
+        keys = np.sort(keys[rng.permutation(keys.size)[:target]])
+    return keys
+
+
+def make_c4(seed=4, m=139255, nnz=19773733):
+    rng = np.random.default_rng(seed)
+    deg_out = rng.lognormal(4.2, 1.3, m)
+    deg_in = rng.lognormal(4.2, 1.3, m)
+    keys = _sample_pairs(rng, deg_out / deg_out.sum(), deg_in / deg_in.sum(), m, nnz)
+    k = rng.geometric(0.3, nnz)
+    vals = np.log1p(k).astype(np.float32)
+    return np.stack([keys // m, keys % m]), vals, (m, m)
+
+
+def make_c3(seed=3, m=50000, nnz=10_000_000):
+    rng = np.random.default_rng(seed)
+    w = 1.0 / np.arange(1, m + 1) ** 1.1
+    pr = rng.permutation(w) / w.sum()
+    pc = rng.permutation(w) / w.sum()
+    keys = _sample_pairs(rng, pr, pc, m, nnz)
+    c = rng.zipf(2.0, nnz)
+    return np.stack([keys // m, keys % m]), np.log1p(c).astype(np.float32), (m, m)
+
+
+def make_c2(seed=2, m=70000, n=784, density=0.19):
+    rng = np.random.default_rng(seed)
+    lo, hi = int(0.2 * n), int(0.8 * n)
+    nnz = int(density * m * n)
+    keys = np.sort(rng.choice(m * (hi - lo), nnz, replace=False))
+    rows, cols = keys // (hi - lo), keys % (hi - lo) + lo
+    big = rng.random(nnz) < 0.4
+    vals = np.where(big, rng.uniform(0.9, 1.0, nnz), rng.uniform(0.0, 0.9, nnz))
+    vals = np.maximum(vals, 1e-3).astype(np.float32)
+    return np.stack([rows, cols]), vals, (m, n)
+
+
+MAKERS = {"c4": make_c4, "c3": make_c3, "c2": make_c2}
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        return False
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------ helpers
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def measure_tf32_matmul(device):
+    """Dense TF32 throughput of torch.matmul (cuBLAS) on this GPU, 8192^3, best of 5."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    a = torch.randn(8192, 8192, device=device)
+    b = torch.randn(8192, 8192, device=device)
+    for _ in range(3):
+        a @ b
+    best = float("inf")
+    for _ in range(5):
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        s.record()
+        a @ b
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b
+    return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
+
+
+def dist_info():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# ------------------------------------------------------------------------------ our arm
+def run_ours(args):
+    from sumac_b200 import SumacConfig, SumacMethod, _native, ops, sumac_factorize
+    from sumac_b200.data import prune_zero_rows_cols
+    from sumac_b200.salsa import SalsaState, draw_perm, init_salsa_factors
+
+    rank, world, local = dist_info()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    cfgd = CONFIGS[args.config]
+    idx_np, val_np, shape = MAKERS[args.config]()
+    idx_h = torch.from_numpy(idx_np)
+    val_h = torch.from_numpy(val_np)
+    d, nb = cfgd["rank"], cfgd["num_blocks"]
+    allow_tf32 = args.precision == "tf32"
+
+    # ---- device-resident timed region (value)
+    S_index = idx_h.to(dev)
+    S_value = val_h.to(dev)
+    S_index, _, _, m, n = prune_zero_rows_cols(S_index, shape)
+    cfg = SumacConfig(method=SumacMethod.SALSA, rank=d, num_blocks=nb, seed=0, verbose=False,
+                      allow_tf32=allow_tf32, device=dev)
+    gen, gen_rows, gen_cols = cfg.get_generator()
+    A, B = init_salsa_factors(S_index, S_value, m, n, d, gen)
+    st = SalsaState(S_index, S_value, m, n, cfg, A, B)
+    for it in range(1, args.warmup + 1):
+        st.iteration(it, draw_perm(m, gen_rows, dev), draw_perm(n, gen_cols, dev))
+    torch.cuda.synchronize()
+    _native.raise_device_error(dev)
+    if world > 1:
+        dist.barrier()
+    lib = _native.lib()
+    launches0 = lib.sumac_kernel_launches()
+    ev0, ev1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    with ClockSampler(local) as clk:
+        ev0.record()
+        for it in range(args.warmup + 1, args.warmup + args.steps + 1):
+            st.iteration(it, draw_perm(m, gen_rows, dev), draw_perm(n, gen_cols, dev))
+        ev1.record()
+        torch.cuda.synchronize()
+    launches = lib.sumac_kernel_launches() - launches0
+    ms = ev0.elapsed_time(ev1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+    _native.raise_device_error(dev)
+    ms_per_step = ms / args.steps
+    value = world * args.steps / (ms * 1e-3)
+
+    # ---- the fused product alone (one B-update of this workload), CUDA events
+    prec = cfg.precision()
+    Dp = ops.padded_rank(d)
+    b = (m + nb - 1) // nb
+    rows = draw_perm(m, gen_rows, dev)[:b]
+    FI = st.Ap[rows].contiguous()
+    x3 = prec == ops.SUMAC_3XTF32
+    ldct = (b + 3) // 4 * 4
+    Ct = torch.zeros((Dp, ldct), device=dev)
+    Ct[:, :b] = torch.randn(b, Dp, device=dev).T * 1e-2
+    if x3:
+        Fhi = (FI.view(torch.int32) & -8192).view(torch.float32)
+        Flo = FI - Fhi
+        Cthi = (Ct.view(torch.int32) & -8192).view(torch.float32)
+        Ctlo = Ct - Cthi
+    else:
+        Fhi, Flo, Cthi, Ctlo = FI, None, Ct, None
+    splits = lib.sumac_relu_product_splits(n, b, Dp, prec)
+    part = torch.empty((splits, n, Dp), device=dev)
+    err = _native.err_word(dev)
+    stream = _native.stream_ptr(dev)
+    P = _native.ptr
+
+    def launch():
+        _native.check(lib.sumac_relu_product(P(st.Bp), n, P(Fhi), P(Flo), P(Cthi), P(Ctlo), ldct,
+                                             b, Dp, prec, P(part), P(err), stream), "relu_product")
+    for _ in range(5):
+        launch()
+    reps = 50
+    k0, k1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    k0.record()
+    for _ in range(reps):
+        launch()
+    k1.record()
+    torch.cuda.synchronize()
+    _native.raise_device_error(dev)
+    kernel_ms = k0.elapsed_time(k1) / reps
+    flops = 4.0 * n * b * d
+    achieved = flops / (kernel_ms * 1e-3) / 1e12
+    pk = peaks()
+    tf32_peak = pk["bf16_tflops"] / 2.0
+    tf32_measured = measure_tf32_matmul(dev) if rank == 0 else None
+
+    # ---- e2e through the public API with host inputs
+    e2e = None
+    if rank == 0 and not args.no_e2e:
+        cfg2 = SumacConfig(method=SumacMethod.SALSA, rank=d, num_blocks=nb, seed=0, verbose=False,
+                           allow_tf32=allow_tf32, max_iterations=args.steps,
+                           eval_interval=args.steps + 1)
+        idx_pin = idx_h.pin_memory()
+        val_pin = val_h.pin_memory()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        A2, B2, _ = sumac_factorize(S_index=idx_pin, S_value=val_pin, shape=shape, config=cfg2)
+        torch.cuda.synchronize()
+        t_e2e = time.perf_counter() - t0
+        h2d = idx_h.numel() * idx_h.element_size() + val_h.numel() * 4
+        d2h = (A2.numel() + B2.numel()) * 4
+        e2e = {"value": args.steps / t_e2e, "unit": "iter/s",
+               "h2d_bytes_per_step": h2d / args.steps, "d2h_bytes_per_step": d2h / args.steps,
+               "seconds": t_e2e, "note": "one sumac_factorize call of `steps` iterations with host "
+               "inputs: copies, validation, pruning, init and CSR setup inside the timed region"}
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    cpu = cpu_baseline(args, idx_np, val_np, shape, d, nb) if not args.no_cpu else None
+    clocks = clk.summary()
+    line = {
+        "metric": "fused ReLU(AB^T)-reduce TFLOP/s; GD/SALSA iters/s at 1/2/4/8 B200",
+        "value": value, "unit": "iter/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak" if world > 1 else "strong", "vs_baseline": None,
+        "dtype": "tf32" if not x3 else "f32 (3xTF32)", "data": "synthetic (seeded stand-in)",
+        "config": {"workload": cfgd["desc"], "m_eff": m, "n_eff": n, "nnz": int(val_np.size),
+                   "rank": d, "num_blocks": nb, "method": "SALSA",
+                   "parallelism": "single GPU" if world == 1 else f"{world} independent replicas",
+                   "l2": "inputs larger than L2 (CSR of both directions ~0.3 GB per step)"},
+        "fused_product": {"tflops": achieved, "ms_per_launch": kernel_ms, "M": n, "N": b, "d": d,
+                          "splits": splits, "flops_per_launch": flops},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
+                     "frac": achieved / tf32_peak, "traffic": None,
+                     "peak_source": f"{pk['source']} bf16 / 2 (dense TF32 rate)",
+                     "tf32_matmul_measured_tflops": tf32_measured},
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "gpu_launches": int(launches),
+    }
+    print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------------------ CPU arms
+def cpu_block_pair_seconds(idx_np, val_np, shape, d, nb, pairs, seed=0):
+    """Time `pairs` SALSA block-update pairs (B against a row block of A, then A against a row
+    block of B) of the CPU oracle at the workload's shapes."""
+    from oracle import sumac_oracle as orc
+    rng = np.random.default_rng(seed)
+    m, n = shape
+    A = np.abs(rng.standard_normal((m, d))) * 0.1
+    B = -np.abs(rng.standard_normal((n, d))) * 0.1
+    dA, dB = np.zeros_like(A), np.zeros_like(B)
+    S_T = idx_np[[1, 0]]
+    times = []
+    for p in range(pairs):
+        perm_r, perm_c = rng.permutation(m), rng.permutation(n)
+        bs_r, bs_c = (m + nb - 1) // nb, (n + nb - 1) // nb
+        in_r = np.zeros(m, bool)
+        in_r[perm_r[:bs_r]] = True
+        in_c = np.zeros(n, bool)
+        in_c[perm_c[:bs_c]] = True
+        set_r = np.nonzero(in_r[idx_np[0]])[0]
+        set_c = np.nonzero(in_c[S_T[0]])[0]
+        t0 = time.perf_counter()
+        B, dB = orc.block_update(A, perm_r[:bs_r], B, dB, idx_np, val_np, set_r, 0.7, 0.3, 0.1)
+        A, dA = orc.block_update(B, perm_c[:bs_c], A, dA, S_T, val_np, set_c, 0.7, 0.3, 0.1)
+        times.append(time.perf_counter() - t0)
+    return times
+
+
+def cpu_baseline(args, idx_np, val_np, shape, d, nb):
+    pairs = 1
+    t = cpu_block_pair_seconds(idx_np, val_np, shape, d, nb, pairs)
+    mean = sum(t) / len(t)
+    return {"value": 1.0 / (nb * mean), "unit": "iter/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{pairs} block-update pairs (1/{nb} of an iteration each) of the numpy "
+                      f"float64 oracle at the workload's shapes, scaled to iterations/s; "
+                      f"reshuffle/CSR cost excluded; numpy BLAS threads = all host cores"}
+
+
+def run_reference(args):
+    rank, world, local = dist_info()
+    if rank != 0:
+        return
+    cfgd = CONFIGS[args.config]
+    idx_np, val_np, shape = MAKERS[args.config]()
+    d, nb = cfgd["rank"], cfgd["num_blocks"]
+    cpu_block_pair_seconds(idx_np, val_np, shape, d, nb, 1)  # warm-up sample
+    times = cpu_block_pair_seconds(idx_np, val_np, shape, d, nb, args.steps)
+    mean = sum(times) / len(times)
+    value = 1.0 / (nb * mean)
+    print(json.dumps({
+        "impl": "reference", "metric": "fused ReLU(AB^T)-reduce TFLOP/s; GD/SALSA iters/s at 1/2/4/8 B200",
+        "value": value, "unit": "iter/s", "n_gpus": world, "steps": args.steps, "warmup": 1,
+        "ms_per_step": mean * 1e3, "higher_is_better": True, "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (seeded stand-in)",
+        "config": {"workload": cfgd["desc"], "rank": d, "num_blocks": nb, "method": "SALSA"},
+        "cpu_baseline": {"value": value, "unit": "iter/s", "cores": os.cpu_count(), "kind": "port",
+                         "sample": f"each step = one SALSA block-update pair (1/{nb} of an "
+                                   "iteration) of the CPU oracle restating the reference's "
+                                   "algorithm, scaled to iterations/s"},
+        "e2e": {"value": value, "unit": "iter/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="c4")
+    ap.add_argument("--precision", choices=["tf32", "3xtf32"], default="tf32")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()
