@@ -81,6 +81,22 @@ int sumac_relu_bat_reduce(const float* A, const float* B, int64_t M, int64_t N, 
                           sumac_stream_t stream);
 
 /*
+ * relu_bat_reduce without a caller workspace. No counterpart in the reference: it exists for
+ * callers that cannot give this library device memory (a host whose allocator owns every byte of
+ * the GPU, such as a MATLAB gpuArray binding or a serving process that reserved the device, or a
+ * path where cudaMalloc / cudaFree must not run because they can synchronise the device). Its
+ * scratch is a fixed 16 MiB array (sumac_noalloc_scratch_bytes()) that lives in the library's
+ * device image on every GPU that loads it until the process exits; larger problems are rejected
+ * with SUMAC_ERR_WORKSPACE. All calls share the array, so calls that overlap on the GPU race. The
+ * first call on a device looks up the array's address and should come before any stream capture.
+ * Same inputs, output and checks as sumac_relu_bat_reduce; it allocates nothing.
+ */
+size_t sumac_noalloc_scratch_bytes(void);
+int sumac_relu_bat_reduce_noalloc(const float* A, const float* B, int64_t M, int64_t N, int D,
+                                  double* out, int precision, int* dev_err,
+                                  sumac_stream_t stream);
+
+/*
  * Masked product on padded operands: Y[M][Dp] = R C with R[j][i] = ReLU(L_ji) off the support and
  * L_ji - S_ij on it, L = X F^T (X: M rows, F and C: N rows). The support of row j is
  * ent[rowptr[j] .. rowptr[j+1]) with int pairs {i, bits of S_ij}. rowptr may be NULL (no support).

@@ -40,6 +40,8 @@ _SIGS = {
     "sumac_relu_bat_c": (i32, [p, p, p, i64, i64, i32, p, i32, p, sz, p, p]),
     "sumac_relu_bat_reduce_workspace_bytes": (sz, [i64, i64, i32, i32]),
     "sumac_relu_bat_reduce": (i32, [p, p, i64, i64, i32, p, i32, p, sz, p, p]),
+    "sumac_noalloc_scratch_bytes": (sz, []),
+    "sumac_relu_bat_reduce_noalloc": (i32, [p, p, i64, i64, i32, p, i32, p, p]),
     "sumac_masked_product_workspace_bytes": (sz, [i64, i64, i32, i32]),
     "sumac_masked_product": (i32, [p, p, p, i64, i64, i32, p, p, p, i32, p, sz, p, p]),
     "sumac_salsa_update_workspace_bytes": (sz, [i64, i64, i32, i32]),

@@ -83,6 +83,11 @@ int64_t round4(int64_t x) { return (x + 3) & ~int64_t(3); }
 
 }  // namespace
 
+namespace sb {
+// Record a message for sumac_last_error() from another translation unit of this library.
+int set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+}  // namespace sb
+
 extern "C" {
 
 int sumac_version(void) { return 1; }
