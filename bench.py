@@ -408,6 +408,55 @@ def run_reference(args):
     }))
 
 
+def run_product_only(args):
+    """The fused product alone at one block update's shapes (rows of the updated factor x one block
+    of the fixed factor), random operands: a small, self-contained case for profiling."""
+    from sumac_b200 import _native, ops
+    dev = torch.device("cuda", 0)
+    cfgd = CONFIGS[args.config]
+    d, nb = cfgd["rank"], cfgd["num_blocks"]
+    M = {"c4": 138963, "c3": 50000, "c2": 70000}[args.config]
+    b = (M + nb - 1) // nb
+    prec = 1 if args.precision == "tf32" else 3
+    Dp = ops.padded_rank(d)
+    g = torch.Generator(device=dev).manual_seed(0)
+    X = torch.zeros((M, Dp), device=dev)
+    X[:, :d] = torch.randn(M, d, device=dev, generator=g)
+    F = torch.zeros((b, Dp), device=dev)
+    F[:, :d] = torch.randn(b, d, device=dev, generator=g)
+    ldct = (b + 3) // 4 * 4
+    Ct = torch.zeros((Dp, ldct), device=dev)
+    Ct[:d, :b] = torch.randn(d, b, device=dev, generator=g)
+    hi = lambda t: (t.view(torch.int32) & -8192).view(torch.float32)  # noqa: E731
+    Fhi, Flo = (hi(F), F - hi(F)) if prec == 3 else (F, None)
+    Chi, Clo = (hi(Ct), Ct - hi(Ct)) if prec == 3 else (Ct, None)
+    lib = _native.lib()
+    splits = lib.sumac_relu_product_splits(M, b, Dp, prec)
+    part = torch.empty((splits, M, Dp), device=dev)
+    P = _native.ptr
+    err = _native.err_word(dev)
+
+    def launch():
+        _native.check(lib.sumac_relu_product(P(X), M, P(Fhi), P(Flo), P(Chi), P(Clo), ldct, b,
+                                             Dp, prec, P(part), P(err),
+                                             _native.stream_ptr(dev)), "relu_product")
+    for _ in range(args.warmup):
+        launch()
+    e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    e0.record()
+    for _ in range(args.steps):
+        launch()
+    e1.record()
+    torch.cuda.synchronize()
+    _native.raise_device_error(dev)
+    ms = e0.elapsed_time(e1) / args.steps
+    tflops = 4.0 * M * b * d / (ms * 1e-3) / 1e12
+    ref = torch.relu(X[:, :d] @ F[:, :d].T) @ Ct[:d, :b].T
+    err_rel = float((part.sum(0)[:, :d] - ref).abs().max() / ref.abs().max())
+    print(json.dumps({"product_only": args.config, "M": M, "N": b, "d": d, "precision": prec,
+                      "ms_per_launch": ms, "tflops": tflops, "max_rel_err_vs_torch": err_rel}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -418,10 +467,14 @@ def main():
     ap.add_argument("--precision", choices=["tf32", "3xtf32"], default="tf32")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--product-only", action="store_true",
+                    help="time the fused product alone at one block update's shapes")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.product_only:
+        run_product_only(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
