@@ -292,7 +292,8 @@ static SalsaPlan plan_salsa(void* ws, int64_t M, int64_t b, int d, int Dp, bool 
   p.P = bp.take<float>((size_t)b * Dp);
   p.Cthi = bp.take<float>((size_t)Dp * p.ldct);
   p.Ctlo = x3 ? bp.take<float>((size_t)Dp * p.ldct) : nullptr;
-  p.gram = bp.take<double>((size_t)gram_parts(b) * d * d);
+  const int gp = gram_parts(b) > salsa_gram_parts(b) ? gram_parts(b) : salsa_gram_parts(b);
+  p.gram = bp.take<double>((size_t)gp * d * d);
   // the split count grows as b shrinks; size for the worst case over b' <= b
   int smax = 1;
   for (int64_t bb = b; bb > 0; bb = bb / 2) {
@@ -330,9 +331,14 @@ int sumac_salsa_block_update(const float* F, int64_t m_fixed, const int64_t* row
   if (!ws || ws_bytes < p.bytes)
     return fail(SUMAC_ERR_WORKSPACE, "salsa_block_update: workspace %zu < %zu", ws_bytes, p.bytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  launch_gather_pad(F, Dp, Dp, rows, b, Dp, p.FI, p.Fhi, p.Flo, s);
-  launch_gram(p.FI, b, d, Dp, p.gram, s);
-  launch_solve(p.FI, b, d, Dp, p.gram, gram_parts(b), p.P, p.Cthi, p.Ctlo, p.ldct, dev_err, s);
+  if (d <= 64) {
+    launch_salsa_prep(F, rows, b, d, Dp, p.FI, p.Fhi, p.Flo, p.P, p.Cthi, p.Ctlo, p.ldct, p.gram,
+                      dev_err, s);
+  } else {
+    launch_gather_pad(F, Dp, Dp, rows, b, Dp, p.FI, p.Fhi, p.Flo, s);
+    launch_gram(p.FI, b, d, Dp, p.gram, s);
+    launch_solve(p.FI, b, d, Dp, p.gram, gram_parts(b), p.P, p.Cthi, p.Ctlo, p.ldct, dev_err, s);
+  }
   int rc = launch_relu_product(X, M, x3 ? p.Fhi : p.FI, p.Flo, p.Cthi, p.Ctlo, p.ldct, b, Dp, x3,
                                p.part, dev_err, sms, g_timeout_ns, s);
   if (rc) return cuda_status(rc, "salsa_block_update");

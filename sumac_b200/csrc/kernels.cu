@@ -243,6 +243,170 @@ void launch_solve(const float* FI, int64_t b, int d, int Dp, const double* gram_
   solve_kernel<<<grid, 128, smem, stream>>>(FI, b, d, Dp, gram_ws, nparts, P, Cthi, Ctlo, ldct, err);
 }
 
+
+// ============================================================================================
+// SALSA prep in two launches (training/salsa.py:138-140):
+//  salsa_gram_kernel   64 gathered rows per CTA: writes F_I (fp32, and tf32 hi / lo halves) and
+//                      the CTA's partial Gram matrix (fp64)
+//  salsa_solve_kernel  every CTA sums the partials in a fixed order, one warp factors G with
+//                      partial pivoting (first maximal |pivot| wins, as LAPACK getrf), and each
+//                      thread solves one row in registers: P[r] = G^{-1} F_I[r] (G symmetric, so
+//                      (G^{-1} F_I^T)^T = F_I G^{-1}); P is written row-major and transposed.
+// ============================================================================================
+static constexpr int PREP_ROWS = 64;
+
+int salsa_gram_parts(int64_t b) { return cdiv64(b, PREP_ROWS) < 1 ? 1 : cdiv64(b, PREP_ROWS); }
+
+__global__ void salsa_gram_kernel(const float* __restrict__ Ffix, const int64_t* __restrict__ rows,
+                                  int64_t b, int d, int Dp, float* __restrict__ FI,
+                                  float* __restrict__ Fhi, float* __restrict__ Flo,
+                                  double* __restrict__ parts) {
+  extern __shared__ float srow[];  // [PREP_ROWS][Dp]
+  const int64_t r0 = (int64_t)blockIdx.x * PREP_ROWS;
+  const int nr = (int)min((int64_t)PREP_ROWS, b - r0);
+  for (int i = threadIdx.x; i < nr * Dp; i += blockDim.x) {
+    const int rr = i / Dp, c = i - rr * Dp;
+    const float v = Ffix[rows[r0 + rr] * Dp + c];
+    srow[i] = v;
+    const int64_t o = (r0 + rr) * Dp + c;
+    FI[o] = v;
+    if (Fhi) {
+      const float h = tf32_hi(v);
+      Fhi[o] = h;
+      Flo[o] = v - h;
+    }
+  }
+  __syncthreads();
+  const int dd = d * d;
+  for (int e = threadIdx.x; e < dd; e += blockDim.x) {
+    const int i = e / d, j = e - i * d;
+    double s = 0.0;
+    for (int rr = 0; rr < nr; ++rr) s += (double)srow[rr * Dp + i] * (double)srow[rr * Dp + j];
+    parts[(size_t)blockIdx.x * dd + e] = s;
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(128) salsa_solve_kernel(const float* __restrict__ FI, int64_t b,
+                                                          int d, int Dp,
+                                                          const double* __restrict__ parts,
+                                                          int nparts, float* __restrict__ P,
+                                                          float* __restrict__ Cthi,
+                                                          float* __restrict__ Ctlo, int64_t ldct,
+                                                          int* err) {
+  __shared__ double sG[D * D];
+  __shared__ int piv[D];
+  const int dd = d * d;
+  for (int e = threadIdx.x; e < dd; e += blockDim.x) {
+    double s = 0.0;
+    for (int q = 0; q < nparts; ++q) s += parts[(size_t)q * dd + e];
+    sG[e] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    for (int k = 0; k < d; ++k) {
+      double best = -1.0;
+      int bi = k;
+      for (int i = k + lane; i < d; i += 32) {
+        const double av = fabs(sG[i * d + k]);
+        if (av > best) { best = av; bi = i; }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const double ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+      }
+      if (lane == 0) {
+        piv[k] = bi;
+        if (best == 0.0 && err && blockIdx.x == 0) atomicCAS(err, 0, DEV_SINGULAR);
+      }
+      if (bi != k)
+        for (int j = lane; j < d; j += 32) {
+          const double tv = sG[k * d + j];
+          sG[k * d + j] = sG[bi * d + j];
+          sG[bi * d + j] = tv;
+        }
+      __syncwarp();
+      const double inv = 1.0 / sG[k * d + k];
+      for (int i = k + 1 + lane; i < d; i += 32) sG[i * d + k] *= inv;
+      __syncwarp();
+      const int rem = d - k - 1;
+      for (int e = lane; e < rem * rem; e += 32) {
+        const int i = k + 1 + e / rem, j = k + 1 + e % rem;
+        sG[i * d + j] -= sG[i * d + k] * sG[k * d + j];
+      }
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= b) return;
+  double x[D];
+#pragma unroll
+  for (int c = 0; c < D; ++c) x[c] = c < d ? (double)FI[r * Dp + c] : 0.0;
+#pragma unroll
+  for (int k = 0; k < D; ++k) {
+    if (k < d) {
+      const int pk = piv[k];
+      // swap x[k] and x[pk] without dynamic register indexing
+#pragma unroll
+      for (int j = 0; j < D; ++j)
+        if (j == pk && j != k) { const double tv = x[k]; x[k] = x[j]; x[j] = tv; }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < D; ++i) {
+    if (i < d) {
+      double s = x[i];
+#pragma unroll
+      for (int j = 0; j < i; ++j) s -= sG[i * d + j] * x[j];
+      x[i] = s;
+    }
+  }
+#pragma unroll
+  for (int i = D - 1; i >= 0; --i) {
+    if (i < d) {
+      double s = x[i];
+#pragma unroll
+      for (int j = i + 1; j < D; ++j)
+        if (j < d) s -= sG[i * d + j] * x[j];
+      x[i] = s / sG[i * d + i];
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < D; ++c) {
+    if (c >= Dp) break;
+    const float v = c < d ? (float)x[c] : 0.f;
+    P[r * Dp + c] = v;
+    if (Ctlo) {
+      const float h = tf32_hi(v);
+      Cthi[c * ldct + r] = h;
+      Ctlo[c * ldct + r] = v - h;
+    } else {
+      Cthi[c * ldct + r] = v;
+    }
+  }
+}
+
+void launch_salsa_prep(const float* Ffix, const int64_t* rows, int64_t b, int d, int Dp, float* FI,
+                       float* Fhi, float* Flo, float* P, float* Cthi, float* Ctlo, int64_t ldct,
+                       double* parts, int* err, cudaStream_t stream) {
+  const int np = salsa_gram_parts(b);
+  count_launch();
+  salsa_gram_kernel<<<np, 256, PREP_ROWS * Dp * sizeof(float), stream>>>(Ffix, rows, b, d, Dp, FI,
+                                                                         Fhi, Flo, parts);
+  const int grid = cdiv64(b, 128);
+  count_launch();
+  if (Dp == 16)
+    salsa_solve_kernel<16><<<grid, 128, 0, stream>>>(FI, b, d, Dp, parts, np, P, Cthi, Ctlo, ldct, err);
+  else if (Dp == 32)
+    salsa_solve_kernel<32><<<grid, 128, 0, stream>>>(FI, b, d, Dp, parts, np, P, Cthi, Ctlo, ldct, err);
+  else
+    salsa_solve_kernel<64><<<grid, 128, 0, stream>>>(FI, b, d, Dp, parts, np, P, Cthi, Ctlo, ldct, err);
+}
+
 // ============================================================================================
 // finalize: Y = sum of split partials + sparse correction, then the per-mode update.
 // Sparse term per entry (i local fixed row, value v), L = <X_j, F_i> in fp32:
@@ -288,36 +452,58 @@ __global__ void finalize_kernel(FinalizeArgs a) {
       int nmax = ne;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) nmax = max(nmax, __shfl_xor_sync(0xffffffffu, nmax, o));
-      for (int q = 0; q < nmax; ++q) {
-        const bool has = q < ne;
-        const int2 en = has ? a.ent[e0 + q] : make_int2(0, 0);
-        const float val = __int_as_float(en.y);
-        const float* frow = a.F + (int64_t)en.x * DP;
-        float part = 0.f;
-        if (has) {
+      // four entries per round: their loads are independent, the accumulation order is fixed
+      for (int q0 = 0; q0 < nmax; q0 += 4) {
+        int2 en[4];
+        float4 f[4][V], c[4][V];
+        float part[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const bool has = q0 + u < ne;
+          en[u] = has ? a.ent[e0 + q0 + u] : make_int2(0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const bool has = q0 + u < ne;
+          const float4* frow = reinterpret_cast<const float4*>(a.F + (int64_t)en[u].x * DP);
+          const float4* crow = reinterpret_cast<const float4*>(a.Cm + (int64_t)en[u].x * DP);
 #pragma unroll
           for (int v = 0; v < V; ++v) {
-            const float4 f = reinterpret_cast<const float4*>(frow)[gl + v * G];
-            part = fmaf(x[v].x, f.x, part);
-            part = fmaf(x[v].y, f.y, part);
-            part = fmaf(x[v].z, f.z, part);
-            part = fmaf(x[v].w, f.w, part);
+            f[u][v] = has ? frow[gl + v * G] : make_float4(0.f, 0.f, 0.f, 0.f);
+            c[u][v] = has ? crow[gl + v * G] : make_float4(0.f, 0.f, 0.f, 0.f);
           }
         }
 #pragma unroll
-        for (int o = G / 2; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
-        if (has) {
-          const float L = part;
-          const float coef = (a.mode == FIN_SALSA) ? (val - L + fmaxf(L, 0.f))
-                                                   : (L - val - fmaxf(L, 0.f));
-          const float* crow = a.Cm + (int64_t)en.x * DP;
+        for (int u = 0; u < 4; ++u) {
+          float s = 0.f;
 #pragma unroll
           for (int v = 0; v < V; ++v) {
-            const float4 c = reinterpret_cast<const float4*>(crow)[gl + v * G];
-            cor[v].x = fmaf(coef, c.x, cor[v].x);
-            cor[v].y = fmaf(coef, c.y, cor[v].y);
-            cor[v].z = fmaf(coef, c.z, cor[v].z);
-            cor[v].w = fmaf(coef, c.w, cor[v].w);
+            s = fmaf(x[v].x, f[u][v].x, s);
+            s = fmaf(x[v].y, f[u][v].y, s);
+            s = fmaf(x[v].z, f[u][v].z, s);
+            s = fmaf(x[v].w, f[u][v].w, s);
+          }
+          part[u] = s;
+        }
+#pragma unroll
+        for (int o = G / 2; o > 0; o >>= 1) {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) part[u] += __shfl_xor_sync(0xffffffffu, part[u], o);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (q0 + u < ne) {
+            const float L = part[u];
+            const float val = __int_as_float(en[u].y);
+            const float coef = (a.mode == FIN_SALSA) ? (val - L + fmaxf(L, 0.f))
+                                                     : (L - val - fmaxf(L, 0.f));
+#pragma unroll
+            for (int v = 0; v < V; ++v) {
+              cor[v].x = fmaf(coef, c[u][v].x, cor[v].x);
+              cor[v].y = fmaf(coef, c[u][v].y, cor[v].y);
+              cor[v].z = fmaf(coef, c[u][v].z, cor[v].z);
+              cor[v].w = fmaf(coef, c[u][v].w, cor[v].w);
+            }
           }
         }
       }

@@ -45,6 +45,14 @@ void launch_gram(const float* FI, int64_t b, int d, int Dp, double* gram_ws, cud
 void launch_solve(const float* FI, int64_t b, int d, int Dp, const double* gram_ws, int nparts,
                   float* P, float* Cthi, float* Ctlo, int64_t ldct, int* err, cudaStream_t stream);
 
+// Gather + Gram + LU + solve for one SALSA block update (d <= 64) in two launches:
+// FI/Fhi/Flo [b][Dp] (Fhi/Flo null in TF32 mode), P [b][Dp], Ct{hi,lo} [Dp][ldct];
+// parts: salsa_gram_parts(b) * d * d doubles of scratch.
+int salsa_gram_parts(int64_t b);
+void launch_salsa_prep(const float* Ffix, const int64_t* rows, int64_t b, int d, int Dp, float* FI,
+                       float* Fhi, float* Flo, float* P, float* Cthi, float* Ctlo, int64_t ldct,
+                       double* parts, int* err, cudaStream_t stream);
+
 // ---- finalize: sparse correction + update -------------------------------------------------
 enum FinalizeMode { FIN_STORE = 0, FIN_SALSA = 1, FIN_GRAD = 2 };
 struct FinalizeArgs {

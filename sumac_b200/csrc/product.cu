@@ -40,46 +40,46 @@ static bool make_map(CUtensorMap* m, const float* base, uint64_t inner, uint64_t
 }
 
 struct ProdCfgRt {
-  int bn, stages;
+  int bn, stages, nxb;
   bool ok;
 };
 
 static ProdCfgRt product_cfg(int Dp, bool x3) {
   if (!x3) {
     switch (Dp) {
-      case 16: return {128, 6, true};
-      case 32: return {128, 4, true};
-      case 64: return {128, 2, true};
-      case 128: return {64, 2, true};
+      case 16: return {128, 6, 2, true};
+      case 32: return {128, 4, 2, true};
+      case 64: return {128, 2, 2, true};
+      case 128: return {64, 2, 1, true};
     }
   } else {
     switch (Dp) {
-      case 16: return {64, 6, true};
-      case 32: return {64, 4, true};
-      case 64: return {64, 2, true};
+      case 16: return {64, 6, 2, true};
+      case 32: return {64, 4, 2, true};
+      case 64: return {64, 2, 1, true};
     }
   }
-  return {0, 0, false};
+  return {0, 0, 0, false};
 }
 
 static ProdCfgRt reduce_cfg(int Dp, bool x3) {
   if (!x3) {
     switch (Dp) {
-      case 16: return {128, 6, true};
-      case 32: return {128, 4, true};
-      case 64: return {128, 3, true};
-      case 128: return {64, 2, true};
-      case 256: return {32, 2, true};
+      case 16: return {128, 6, 2, true};
+      case 32: return {128, 4, 2, true};
+      case 64: return {128, 3, 2, true};
+      case 128: return {64, 2, 2, true};
+      case 256: return {32, 2, 1, true};
     }
   } else {
     switch (Dp) {
-      case 16: return {128, 4, true};
-      case 32: return {128, 3, true};
-      case 64: return {64, 3, true};
-      case 128: return {32, 2, true};
+      case 16: return {128, 4, 2, true};
+      case 32: return {128, 3, 2, true};
+      case 64: return {64, 3, 1, true};
+      case 128: return {32, 2, 1, true};
     }
   }
-  return {0, 0, false};
+  return {0, 0, 0, false};
 }
 
 bool product_supported(int Dp, bool x3) { return product_cfg(Dp, x3).ok; }
@@ -114,12 +114,12 @@ int product_split_count(int64_t M, int64_t N, int Dp, bool x3, int num_sms) {
   return s;
 }
 
-template <int DP, int BN, int STAGES, bool X3, bool REDUCE>
+template <int DP, int BN, int STAGES, bool X3, bool REDUCE, int NXB>
 static int run_kernel(const CUtensorMap& mx, const CUtensorMap& mfh, const CUtensorMap& mfl,
                       const CUtensorMap& mch, const CUtensorMap& mcl, const ProductParams& p,
                       int grid, cudaStream_t stream) {
-  using Cfg = ProductCfg<DP, BN, STAGES, X3, REDUCE>;
-  auto kern = relu_product_kernel<DP, BN, STAGES, X3, REDUCE>;
+  using Cfg = ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>;
+  auto kern = relu_product_kernel<DP, BN, STAGES, X3, REDUCE, NXB>;
   cudaError_t e =
       cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
   if (e != cudaSuccess) return (int)e;
@@ -128,37 +128,37 @@ static int run_kernel(const CUtensorMap& mx, const CUtensorMap& mfh, const CUten
   return (int)cudaGetLastError();
 }
 
-#define SB_PRODUCT_CASE(DPV, BNV, STV, X3V, REDV)                                              \
-  if (Dp == DPV && bn == BNV && stages == STV && x3 == X3V)                                    \
-    return run_kernel<DPV, BNV, STV, X3V, REDV>(mx, mfh, mfl, mch, mcl, p, grid, stream);
+#define SB_PRODUCT_CASE(DPV, BNV, STV, X3V, REDV, NXBV)                                        \
+  if (Dp == DPV && bn == BNV && stages == STV && x3 == X3V && nxb == NXBV)                     \
+    return run_kernel<DPV, BNV, STV, X3V, REDV, NXBV>(mx, mfh, mfl, mch, mcl, p, grid, stream);
 
-static int dispatch_product(int Dp, int bn, int stages, bool x3, const CUtensorMap& mx,
+static int dispatch_product(int Dp, int bn, int stages, int nxb, bool x3, const CUtensorMap& mx,
                             const CUtensorMap& mfh, const CUtensorMap& mfl, const CUtensorMap& mch,
                             const CUtensorMap& mcl, const ProductParams& p, int grid,
                             cudaStream_t stream) {
-  SB_PRODUCT_CASE(16, 128, 6, false, false)
-  SB_PRODUCT_CASE(32, 128, 4, false, false)
-  SB_PRODUCT_CASE(64, 128, 2, false, false)
-  SB_PRODUCT_CASE(128, 64, 2, false, false)
-  SB_PRODUCT_CASE(16, 64, 6, true, false)
-  SB_PRODUCT_CASE(32, 64, 4, true, false)
-  SB_PRODUCT_CASE(64, 64, 2, true, false)
+  SB_PRODUCT_CASE(16, 128, 6, false, false, 2)
+  SB_PRODUCT_CASE(32, 128, 4, false, false, 2)
+  SB_PRODUCT_CASE(64, 128, 2, false, false, 2)
+  SB_PRODUCT_CASE(128, 64, 2, false, false, 1)
+  SB_PRODUCT_CASE(16, 64, 6, true, false, 2)
+  SB_PRODUCT_CASE(32, 64, 4, true, false, 2)
+  SB_PRODUCT_CASE(64, 64, 2, true, false, 1)
   return -1;
 }
 
-static int dispatch_reduce(int Dp, int bn, int stages, bool x3, const CUtensorMap& mx,
+static int dispatch_reduce(int Dp, int bn, int stages, int nxb, bool x3, const CUtensorMap& mx,
                            const CUtensorMap& mfh, const CUtensorMap& mfl, const CUtensorMap& mch,
                            const CUtensorMap& mcl, const ProductParams& p, int grid,
                            cudaStream_t stream) {
-  SB_PRODUCT_CASE(16, 128, 6, false, true)
-  SB_PRODUCT_CASE(32, 128, 4, false, true)
-  SB_PRODUCT_CASE(64, 128, 3, false, true)
-  SB_PRODUCT_CASE(128, 64, 2, false, true)
-  SB_PRODUCT_CASE(256, 32, 2, false, true)
-  SB_PRODUCT_CASE(16, 128, 4, true, true)
-  SB_PRODUCT_CASE(32, 128, 3, true, true)
-  SB_PRODUCT_CASE(64, 64, 3, true, true)
-  SB_PRODUCT_CASE(128, 32, 2, true, true)
+  SB_PRODUCT_CASE(16, 128, 6, false, true, 2)
+  SB_PRODUCT_CASE(32, 128, 4, false, true, 2)
+  SB_PRODUCT_CASE(64, 128, 3, false, true, 2)
+  SB_PRODUCT_CASE(128, 64, 2, false, true, 2)
+  SB_PRODUCT_CASE(256, 32, 2, false, true, 1)
+  SB_PRODUCT_CASE(16, 128, 4, true, true, 2)
+  SB_PRODUCT_CASE(32, 128, 3, true, true, 2)
+  SB_PRODUCT_CASE(64, 64, 3, true, true, 1)
+  SB_PRODUCT_CASE(128, 32, 2, true, true, 1)
   return -1;
 }
 #undef SB_PRODUCT_CASE
@@ -192,7 +192,7 @@ int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float
   p.timeout_ns = timeout_ns;
   const int64_t items = (int64_t)p.n_tiles * p.splits;
   const int grid = (int)(items < num_sms ? items : num_sms);
-  return dispatch_product(Dp, c.bn, c.stages, x3, mx, mfh, mfl, mch, mcl, p, grid, stream);
+  return dispatch_product(Dp, c.bn, c.stages, c.nxb, x3, mx, mfh, mfl, mch, mcl, p, grid, stream);
 }
 
 int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float* Flo, int64_t N,
@@ -218,7 +218,7 @@ int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float*
   const int64_t items = (int64_t)p.n_tiles * p.splits;
   const int grid = (int)(items < num_sms ? items : num_sms);
   *grid_out = grid;
-  return dispatch_reduce(Dp, c.bn, c.stages, x3, mx, mfh, mfl, mfh, mfh, p, grid, stream);
+  return dispatch_reduce(Dp, c.bn, c.stages, c.nxb, x3, mx, mfh, mfl, mfh, mfh, p, grid, stream);
 }
 
 }  // namespace sb

@@ -193,6 +193,49 @@ __device__ __forceinline__ void tmem_ld_wait_regs32(float* v) {
                :
                : "memory");
 }
+// 32 lanes x 32 bit, 32 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t* r = reinterpret_cast<uint32_t*>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+  const uint32_t* r = reinterpret_cast<const uint32_t*>(v);
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+// Wait for tcgen05.ld with N registers tied to the wait (N a multiple of 32).
+template <int N>
+__device__ __forceinline__ void tmem_ld_wait_all(float* v) {
+#pragma unroll
+  for (int i = 0; i < N; i += 32) {
+    if (i == 0) tmem_ld_wait_regs32(v);
+    else asm volatile("" : "+f"(v[i]), "+f"(v[i + 1]), "+f"(v[i + 2]), "+f"(v[i + 3]), "+f"(v[i + 4]),
+                     "+f"(v[i + 5]), "+f"(v[i + 6]), "+f"(v[i + 7]), "+f"(v[i + 8]), "+f"(v[i + 9]),
+                     "+f"(v[i + 10]), "+f"(v[i + 11]), "+f"(v[i + 12]), "+f"(v[i + 13]),
+                     "+f"(v[i + 14]), "+f"(v[i + 15]), "+f"(v[i + 16]), "+f"(v[i + 17]),
+                     "+f"(v[i + 18]), "+f"(v[i + 19]), "+f"(v[i + 20]), "+f"(v[i + 21]),
+                     "+f"(v[i + 22]), "+f"(v[i + 23]), "+f"(v[i + 24]), "+f"(v[i + 25]),
+                     "+f"(v[i + 26]), "+f"(v[i + 27]), "+f"(v[i + 28]), "+f"(v[i + 29]),
+                     "+f"(v[i + 30]), "+f"(v[i + 31])::"memory");
+  }
+}
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
