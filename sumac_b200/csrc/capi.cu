@@ -263,15 +263,16 @@ int sumac_masked_product(const float* X, const float* F, const float* C, int64_t
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (x3) launch_gather_pad(F, Dp, Dp, nullptr, N, Dp, nullptr, p.Fhi, p.Flo, s);
   launch_transpose_split(C, N, Dp, p.Cthi, p.Ctlo, p.ldct, s);
-  int rc = launch_relu_product(X, M, x3 ? p.Fhi : F, p.Flo, p.Cthi, p.Ctlo, p.ldct, N, Dp, x3,
-                               p.part, dev_err, sms, g_timeout_ns, s);
-  if (rc) return cuda_status(rc, "masked_product");
   FinalizeArgs f{};
   f.mode = FIN_STORE; f.M = M; f.Dp = Dp; f.splits = product_split_count(M, N, Dp, x3, sms);
   f.ws = p.part; f.X = const_cast<float*>(X); f.F = F; f.Cm = C;
   f.rowptr = rowptr; f.ent = reinterpret_cast<const int2*>(ent);
   f.out = Y; f.out_d = Dp; f.ld_out = Dp;
-  launch_finalize(f, s);
+  int fused = 0;
+  int rc = launch_relu_product(X, M, x3 ? p.Fhi : F, p.Flo, p.Cthi, p.Ctlo, p.ldct, N, Dp, x3,
+                               p.part, dev_err, sms, g_timeout_ns, s, &f, &fused);
+  if (rc) return cuda_status(rc, "masked_product");
+  if (!fused) launch_finalize(f, s);
   return launched("masked_product");
 }
 
@@ -279,6 +280,7 @@ int sumac_masked_product(const float* X, const float* F, const float* C, int64_t
 struct SalsaPlan {
   float *FI, *Fhi, *Flo, *P, *Cthi, *Ctlo, *part;
   double* gram;
+  unsigned int* counter;
   int64_t ldct;
   size_t bytes;
 };
@@ -292,8 +294,10 @@ static SalsaPlan plan_salsa(void* ws, int64_t M, int64_t b, int d, int Dp, bool 
   p.P = bp.take<float>((size_t)b * Dp);
   p.Cthi = bp.take<float>((size_t)Dp * p.ldct);
   p.Ctlo = x3 ? bp.take<float>((size_t)Dp * p.ldct) : nullptr;
-  const int gp = gram_parts(b) > salsa_gram_parts(b) ? gram_parts(b) : salsa_gram_parts(b);
-  p.gram = bp.take<double>((size_t)gp * d * d);
+  const size_t gbytes = (size_t)gram_parts(b) * d * d * sizeof(double);
+  const size_t pbytes = salsa_prep_scratch_bytes(b, d);
+  p.gram = bp.take<double>(((gbytes > pbytes ? gbytes : pbytes) + 7) / 8);
+  p.counter = bp.take<unsigned int>(64);
   // the split count grows as b shrinks; size for the worst case over b' <= b
   int smax = 1;
   for (int64_t bb = b; bb > 0; bb = bb / 2) {
@@ -331,23 +335,25 @@ int sumac_salsa_block_update(const float* F, int64_t m_fixed, const int64_t* row
   if (!ws || ws_bytes < p.bytes)
     return fail(SUMAC_ERR_WORKSPACE, "salsa_block_update: workspace %zu < %zu", ws_bytes, p.bytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (d <= 64) {
+  if (d <= 32) {
+    cudaMemsetAsync(p.counter, 0, sizeof(unsigned int), s);
     launch_salsa_prep(F, rows, b, d, Dp, p.FI, p.Fhi, p.Flo, p.P, p.Cthi, p.Ctlo, p.ldct, p.gram,
-                      dev_err, s);
+                      p.counter, dev_err, s);
   } else {
     launch_gather_pad(F, Dp, Dp, rows, b, Dp, p.FI, p.Fhi, p.Flo, s);
     launch_gram(p.FI, b, d, Dp, p.gram, s);
     launch_solve(p.FI, b, d, Dp, p.gram, gram_parts(b), p.P, p.Cthi, p.Ctlo, p.ldct, dev_err, s);
   }
-  int rc = launch_relu_product(X, M, x3 ? p.Fhi : p.FI, p.Flo, p.Cthi, p.Ctlo, p.ldct, b, Dp, x3,
-                               p.part, dev_err, sms, g_timeout_ns, s);
-  if (rc) return cuda_status(rc, "salsa_block_update");
   FinalizeArgs f{};
   f.mode = FIN_SALSA; f.M = M; f.Dp = Dp; f.splits = product_split_count(M, b, Dp, x3, sms);
   f.ws = p.part; f.X = X; f.dX = dX; f.F = p.FI; f.Cm = p.P;
   f.rowptr = rowptr; f.ent = reinterpret_cast<const int2*>(ent);
   f.momentum = momentum; f.lrate = lrate; f.unbias = unbias;
-  launch_finalize(f, s);
+  int fused = 0;
+  int rc = launch_relu_product(X, M, x3 ? p.Fhi : p.FI, p.Flo, p.Cthi, p.Ctlo, p.ldct, b, Dp, x3,
+                               p.part, dev_err, sms, g_timeout_ns, s, nullptr, &fused);
+  if (rc) return cuda_status(rc, "salsa_block_update");
+  if (!fused) launch_finalize(f, s);
   return launched("salsa_block_update");
 }
 
@@ -433,15 +439,16 @@ int sumac_gd_block_grad(const float* A, const float* B, int64_t n, int d, const 
   // pass B: rows j of B, contraction over the b block rows; C = A_I
   launch_gather_pad(A, Dp, Dp, rows, b, Dp, p.AI, p.AIhi, p.AIlo, s);
   launch_transpose_split(p.AI, b, Dp, p.AIthi, p.AItlo, p.ldb, s);
-  int rc = launch_relu_product(B, n, x3 ? p.AIhi : p.AI, p.AIlo, p.AIthi, p.AItlo, p.ldb, b, Dp,
-                               x3, p.part, dev_err, sms, g_timeout_ns, s);
-  if (rc) return cuda_status(rc, "gd_block_grad (B pass)");
   FinalizeArgs f{};
   f.mode = FIN_GRAD; f.M = n; f.Dp = Dp; f.splits = product_split_count(n, b, Dp, x3, sms);
   f.ws = p.part; f.X = const_cast<float*>(B); f.F = p.AI; f.Cm = p.AI;
   f.rowptr = rowptr_b; f.ent = reinterpret_cast<const int2*>(ent_b);
   f.out = gB; f.scale = 2.f; f.accumulate = accumulate;
-  launch_finalize(f, s);
+  int fused = 0;
+  int rc = launch_relu_product(B, n, x3 ? p.AIhi : p.AI, p.AIlo, p.AIthi, p.AItlo, p.ldb, b, Dp,
+                               x3, p.part, dev_err, sms, g_timeout_ns, s, nullptr, &fused);
+  if (rc) return cuda_status(rc, "gd_block_grad (B pass)");
+  if (!fused) launch_finalize(f, s);
   // pass A: rows i of A_I, contraction over all n rows of B; C = B
   if (x3) launch_gather_pad(B, Dp, Dp, nullptr, n, Dp, nullptr, p.Bhi, p.Blo, s);
   launch_transpose_split(B, n, Dp, p.Bthi, p.Btlo, p.ldn, s);

@@ -257,11 +257,62 @@ static constexpr int PREP_ROWS = 64;
 
 int salsa_gram_parts(int64_t b) { return cdiv64(b, PREP_ROWS) < 1 ? 1 : cdiv64(b, PREP_ROWS); }
 
+// Register LU with partial pivoting of the D x D matrix G (padded with an identity block),
+// by one warp: lane i holds row i, the pivot row is broadcast by shuffles. Writes the packed L\U
+// factors and the pivot sequence (first maximal |pivot| wins, as LAPACK getrf).
+template <int D>
+__device__ __forceinline__ void warp_lu(const double* __restrict__ G, int d, double* LU, int* piv,
+                                        int* err) {
+  static_assert(D <= 32, "one row per lane");
+  const int lane = threadIdx.x & 31;
+  double a[D];
+#pragma unroll
+  for (int j = 0; j < D; ++j)
+    a[j] = (lane < d && j < d) ? G[lane * d + j] : (lane == j ? 1.0 : 0.0);
+#pragma unroll
+  for (int k = 0; k < D; ++k) {
+    double best = (lane >= k && lane < D) ? fabs(a[k]) : -1.0;
+    int bi = lane;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const double ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+    }
+    if (lane == 0) {
+      piv[k] = bi;
+      if (best == 0.0 && err) atomicCAS(err, 0, DEV_SINGULAR);
+    }
+    const int src = lane == k ? bi : (lane == bi ? k : lane);
+#pragma unroll
+    for (int j = 0; j < D; ++j) a[j] = __shfl_sync(0xffffffffu, a[j], src);
+    double u[D];
+#pragma unroll
+    for (int j = k; j < D; ++j) u[j] = __shfl_sync(0xffffffffu, a[j], k);
+    if (lane > k && lane < D) {
+      const double l = a[k] / u[k];
+      a[k] = l;
+#pragma unroll
+      for (int j = k + 1; j < D; ++j) a[j] -= l * u[j];
+    }
+  }
+  if (lane < D) {
+#pragma unroll
+    for (int j = 0; j < D; ++j) LU[lane * D + j] = a[j];
+  }
+}
+
+// 64 gathered rows per CTA: F_I (fp32 and tf32 hi / lo halves) and the CTA's partial Gram
+// (fp64). The last CTA to finish sums the partials in a fixed order and factors G.
+template <int D>
 __global__ void salsa_gram_kernel(const float* __restrict__ Ffix, const int64_t* __restrict__ rows,
                                   int64_t b, int d, int Dp, float* __restrict__ FI,
                                   float* __restrict__ Fhi, float* __restrict__ Flo,
-                                  double* __restrict__ parts) {
+                                  double* __restrict__ parts, unsigned int* counter,
+                                  double* __restrict__ LU, int* __restrict__ piv, int* err) {
   extern __shared__ float srow[];  // [PREP_ROWS][Dp]
+  __shared__ double sG[D * D];
+  __shared__ bool last;
   const int64_t r0 = (int64_t)blockIdx.x * PREP_ROWS;
   const int nr = (int)min((int64_t)PREP_ROWS, b - r0);
   for (int i = threadIdx.x; i < nr * Dp; i += blockDim.x) {
@@ -284,62 +335,36 @@ __global__ void salsa_gram_kernel(const float* __restrict__ Ffix, const int64_t*
     for (int rr = 0; rr < nr; ++rr) s += (double)srow[rr * Dp + i] * (double)srow[rr * Dp + j];
     parts[(size_t)blockIdx.x * dd + e] = s;
   }
-}
-
-template <int D>
-__global__ void __launch_bounds__(128) salsa_solve_kernel(const float* __restrict__ FI, int64_t b,
-                                                          int d, int Dp,
-                                                          const double* __restrict__ parts,
-                                                          int nparts, float* __restrict__ P,
-                                                          float* __restrict__ Cthi,
-                                                          float* __restrict__ Ctlo, int64_t ldct,
-                                                          int* err) {
-  __shared__ double sG[D * D];
-  __shared__ int piv[D];
-  const int dd = d * d;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
   for (int e = threadIdx.x; e < dd; e += blockDim.x) {
     double s = 0.0;
-    for (int q = 0; q < nparts; ++q) s += parts[(size_t)q * dd + e];
+#pragma unroll 4
+    for (int q = 0; q < (int)gridDim.x; ++q) s += __ldcg(&parts[(size_t)q * dd + e]);
     sG[e] = s;
   }
   __syncthreads();
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    for (int k = 0; k < d; ++k) {
-      double best = -1.0;
-      int bi = k;
-      for (int i = k + lane; i < d; i += 32) {
-        const double av = fabs(sG[i * d + k]);
-        if (av > best) { best = av; bi = i; }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const double ob = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
-      }
-      if (lane == 0) {
-        piv[k] = bi;
-        if (best == 0.0 && err && blockIdx.x == 0) atomicCAS(err, 0, DEV_SINGULAR);
-      }
-      if (bi != k)
-        for (int j = lane; j < d; j += 32) {
-          const double tv = sG[k * d + j];
-          sG[k * d + j] = sG[bi * d + j];
-          sG[bi * d + j] = tv;
-        }
-      __syncwarp();
-      const double inv = 1.0 / sG[k * d + k];
-      for (int i = k + 1 + lane; i < d; i += 32) sG[i * d + k] *= inv;
-      __syncwarp();
-      const int rem = d - k - 1;
-      for (int e = lane; e < rem * rem; e += 32) {
-        const int i = k + 1 + e / rem, j = k + 1 + e % rem;
-        sG[i * d + j] -= sG[i * d + k] * sG[k * d + j];
-      }
-      __syncwarp();
-    }
-  }
+  if (threadIdx.x < 32) warp_lu<D>(sG, d, LU, piv, err);
+  if (threadIdx.x == 0) *counter = 0u;  // ready for the next launch (graph replays included)
+}
+
+// P[r] = G^{-1} F_I[r] from the packed LU factors; one thread per row, in registers.
+template <int D>
+__global__ void __launch_bounds__(128) salsa_solve_kernel(const float* __restrict__ FI, int64_t b,
+                                                          int d, int Dp,
+                                                          const double* __restrict__ LU,
+                                                          const int* __restrict__ piv_g,
+                                                          float* __restrict__ P,
+                                                          float* __restrict__ Cthi,
+                                                          float* __restrict__ Ctlo, int64_t ldct) {
+  __shared__ double sLU[D][D + 1];
+  __shared__ int piv[D];
+  for (int e = threadIdx.x; e < D * D; e += blockDim.x) sLU[e / D][e % D] = LU[e];
+  if (threadIdx.x < D) piv[threadIdx.x] = piv_g[threadIdx.x];
   __syncthreads();
   const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= b) return;
@@ -348,36 +373,27 @@ __global__ void __launch_bounds__(128) salsa_solve_kernel(const float* __restric
   for (int c = 0; c < D; ++c) x[c] = c < d ? (double)FI[r * Dp + c] : 0.0;
 #pragma unroll
   for (int k = 0; k < D; ++k) {
-    if (k < d) {
-      const int pk = piv[k];
-      // swap x[k] and x[pk] without dynamic register indexing
+    const int pk = piv[k];
 #pragma unroll
-      for (int j = 0; j < D; ++j)
-        if (j == pk && j != k) { const double tv = x[k]; x[k] = x[j]; x[j] = tv; }
-    }
+    for (int j = k + 1; j < D; ++j)
+      if (j == pk) { const double tv = x[k]; x[k] = x[j]; x[j] = tv; }
   }
 #pragma unroll
-  for (int i = 0; i < D; ++i) {
-    if (i < d) {
-      double s = x[i];
+  for (int i = 1; i < D; ++i) {
+    double s = x[i];
 #pragma unroll
-      for (int j = 0; j < i; ++j) s -= sG[i * d + j] * x[j];
-      x[i] = s;
-    }
+    for (int j = 0; j < i; ++j) s -= sLU[i][j] * x[j];
+    x[i] = s;
   }
 #pragma unroll
   for (int i = D - 1; i >= 0; --i) {
-    if (i < d) {
-      double s = x[i];
+    double s = x[i];
 #pragma unroll
-      for (int j = i + 1; j < D; ++j)
-        if (j < d) s -= sG[i * d + j] * x[j];
-      x[i] = s / sG[i * d + i];
-    }
+    for (int j = i + 1; j < D; ++j) s -= sLU[i][j] * x[j];
+    x[i] = s / sLU[i][i];
   }
 #pragma unroll
   for (int c = 0; c < D; ++c) {
-    if (c >= Dp) break;
     const float v = c < d ? (float)x[c] : 0.f;
     P[r * Dp + c] = v;
     if (Ctlo) {
@@ -390,21 +406,33 @@ __global__ void __launch_bounds__(128) salsa_solve_kernel(const float* __restric
   }
 }
 
+size_t salsa_prep_scratch_bytes(int64_t b, int d) {
+  const int D = d <= 16 ? 16 : 32;
+  return (size_t)salsa_gram_parts(b) * d * d * sizeof(double) + D * D * sizeof(double) +
+         64 * sizeof(int) + 64;
+}
+
 void launch_salsa_prep(const float* Ffix, const int64_t* rows, int64_t b, int d, int Dp, float* FI,
                        float* Fhi, float* Flo, float* P, float* Cthi, float* Ctlo, int64_t ldct,
-                       double* parts, int* err, cudaStream_t stream) {
+                       void* scratch, unsigned int* counter, int* err, cudaStream_t stream) {
   const int np = salsa_gram_parts(b);
-  count_launch();
-  salsa_gram_kernel<<<np, 256, PREP_ROWS * Dp * sizeof(float), stream>>>(Ffix, rows, b, d, Dp, FI,
-                                                                         Fhi, Flo, parts);
+  const int D = Dp;
+  double* parts = reinterpret_cast<double*>(scratch);
+  double* LU = parts + (size_t)np * d * d;
+  int* piv = reinterpret_cast<int*>(LU + D * D);
+  const size_t smem = PREP_ROWS * Dp * sizeof(float);
   const int grid = cdiv64(b, 128);
   count_launch();
-  if (Dp == 16)
-    salsa_solve_kernel<16><<<grid, 128, 0, stream>>>(FI, b, d, Dp, parts, np, P, Cthi, Ctlo, ldct, err);
-  else if (Dp == 32)
-    salsa_solve_kernel<32><<<grid, 128, 0, stream>>>(FI, b, d, Dp, parts, np, P, Cthi, Ctlo, ldct, err);
-  else
-    salsa_solve_kernel<64><<<grid, 128, 0, stream>>>(FI, b, d, Dp, parts, np, P, Cthi, Ctlo, ldct, err);
+  count_launch();
+  if (D == 16) {
+    salsa_gram_kernel<16><<<np, 256, smem, stream>>>(Ffix, rows, b, d, Dp, FI, Fhi, Flo, parts,
+                                                     counter, LU, piv, err);
+    salsa_solve_kernel<16><<<grid, 128, 0, stream>>>(FI, b, d, Dp, LU, piv, P, Cthi, Ctlo, ldct);
+  } else {
+    salsa_gram_kernel<32><<<np, 256, smem, stream>>>(Ffix, rows, b, d, Dp, FI, Fhi, Flo, parts,
+                                                     counter, LU, piv, err);
+    salsa_solve_kernel<32><<<grid, 128, 0, stream>>>(FI, b, d, Dp, LU, piv, P, Cthi, Ctlo, ldct);
+  }
 }
 
 // ============================================================================================
@@ -771,8 +799,11 @@ int launch_block_csr(const int64_t* perm, int64_t m_fixed, int num_blocks, const
     count_launch();
     scan_exclusive_kernel<<<1, 1024, 0, stream>>>(hist, (int64_t)num_blocks * L.ncta);
     const size_t smem = (size_t)9 * num_blocks * sizeof(int);
-    if (smem > 48 * 1024)
+    static int scatter_smem_set = 0;  // largest opt-in so far (set eagerly before any capture)
+    if (smem > 48 * 1024 && (int)smem > scatter_smem_set) {
       cudaFuncSetAttribute(csr_scatter_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      scatter_smem_set = (int)smem;
+    }
     count_launch();
     csr_scatter_kernel<<<L.ncta, CSR_THREADS, smem, stream>>>(e_fixed, e_out, e_val, nnz, L.chunk,
                                                              inv, bs, num_blocks, M, hist, keys, ent);

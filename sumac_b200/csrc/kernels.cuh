@@ -15,10 +15,14 @@ long long launch_count();
 // X [M][Dp], F{hi,lo} [N][Dp], Ct{hi,lo} [Dp][ldct] (row-major, 16-byte aligned rows).
 // Writes ws[splits][M][Dp] partial products (splits = product_split_count(...)). Returns 0 or a
 // cudaError_t value; -1 for an unsupported (Dp, x3) combination, -5 bad sizes, -6 tensor map.
+struct FinalizeArgs;
+// With fin != nullptr and a single split (product_split_count == 1) and Dp <= 32, the epilogue
+// applies the finalize pass itself and ws is not written; returns 1 in *fused in that case.
 int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float* Flo,
                         const float* Cthi, const float* Ctlo, int64_t ldct, int64_t N, int Dp,
                         bool x3, float* ws, int* err, int num_sms, unsigned long long timeout_ns,
-                        cudaStream_t stream);
+                        cudaStream_t stream, const FinalizeArgs* fin = nullptr,
+                        int* fused = nullptr);
 // Reduce mode: partials[grid][2] (grid <= num_sms) hold per-CTA (sum ReLU, sum ReLU^2).
 int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float* Flo, int64_t N,
                        int Dp, bool x3, double* partials, int* grid_out, int* err, int num_sms,
@@ -45,13 +49,15 @@ void launch_gram(const float* FI, int64_t b, int d, int Dp, double* gram_ws, cud
 void launch_solve(const float* FI, int64_t b, int d, int Dp, const double* gram_ws, int nparts,
                   float* P, float* Cthi, float* Ctlo, int64_t ldct, int* err, cudaStream_t stream);
 
-// Gather + Gram + LU + solve for one SALSA block update (d <= 64) in two launches:
-// FI/Fhi/Flo [b][Dp] (Fhi/Flo null in TF32 mode), P [b][Dp], Ct{hi,lo} [Dp][ldct];
-// parts: salsa_gram_parts(b) * d * d doubles of scratch.
+// Gather + Gram + LU + solve for one SALSA block update (d <= 32) in two launches:
+// FI/Fhi/Flo [b][Dp] (Fhi/Flo null in TF32 mode), P [b][Dp], Ct{hi,lo} [Dp][ldct].
+// scratch: salsa_prep_scratch_bytes(b, d); counter: a device word that is zero before the first
+// launch (the kernels leave it zero).
 int salsa_gram_parts(int64_t b);
+size_t salsa_prep_scratch_bytes(int64_t b, int d);
 void launch_salsa_prep(const float* Ffix, const int64_t* rows, int64_t b, int d, int Dp, float* FI,
                        float* Fhi, float* Flo, float* P, float* Cthi, float* Ctlo, int64_t ldct,
-                       double* parts, int* err, cudaStream_t stream);
+                       void* scratch, unsigned int* counter, int* err, cudaStream_t stream);
 
 // ---- finalize: sparse correction + update -------------------------------------------------
 enum FinalizeMode { FIN_STORE = 0, FIN_SALSA = 1, FIN_GRAD = 2 };

@@ -1,5 +1,7 @@
 // product.cu — tensor maps, the (Dp, precision) configuration table and launchers of the fused
 // ReLU product / reduce kernel (relu_product.cuh).
+#include <cstring>
+
 #include "kernels.cuh"
 #include "relu_product.cuh"
 
@@ -120,9 +122,16 @@ static int run_kernel(const CUtensorMap& mx, const CUtensorMap& mfh, const CUten
                       int grid, cudaStream_t stream) {
   using Cfg = ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>;
   auto kern = relu_product_kernel<DP, BN, STAGES, X3, REDUCE, NXB>;
-  cudaError_t e =
-      cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
-  if (e != cudaSuccess) return (int)e;
+  // once per device (and before any stream capture: the first call of a shape runs eagerly)
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return (int)e;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
   count_launch();
   kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(mx, mfh, mfl, mch, mcl, p);
   return (int)cudaGetLastError();
@@ -170,7 +179,7 @@ static CUtensorMapSwizzle row_swizzle(int Dp) {
 int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float* Flo,
                         const float* Cthi, const float* Ctlo, int64_t ldct, int64_t N, int Dp,
                         bool x3, float* ws, int* err, int num_sms, unsigned long long timeout_ns,
-                        cudaStream_t stream) {
+                        cudaStream_t stream, const FinalizeArgs* fin, int* fused) {
   ProdCfgRt c = product_cfg(Dp, x3);
   if (!c.ok) return -1;
   if (M <= 0 || N <= 0 || M >= INT32_MAX || N >= INT32_MAX) return -5;
@@ -190,6 +199,10 @@ int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float
   p.partials = nullptr;
   p.err = err;
   p.timeout_ns = timeout_ns;
+  p.fuse = (fin != nullptr && p.splits == 1 && Dp <= 32) ? 1 : 0;
+  if (p.fuse) p.fin = *fin;
+  else memset(&p.fin, 0, sizeof(p.fin));
+  if (fused) *fused = p.fuse;
   const int64_t items = (int64_t)p.n_tiles * p.splits;
   const int grid = (int)(items < num_sms ? items : num_sms);
   return dispatch_product(Dp, c.bn, c.stages, c.nxb, x3, mx, mfh, mfl, mch, mcl, p, grid, stream);
@@ -212,6 +225,8 @@ int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float*
   p.N = (int)N;
   plan_splits(M, N, c.bn, num_sms, &p.splits, &p.chunks_per_split, &p.n_chunks, &p.n_tiles);
   p.ws = nullptr;
+  p.fuse = 0;
+  memset(&p.fin, 0, sizeof(p.fin));
   p.partials = partials;
   p.err = err;
   p.timeout_ns = timeout_ns;

@@ -34,6 +34,7 @@
 // SWIZZLE_64B, 128 B rows: SWIZZLE_128B; wider rows are split in 128 B sub-tiles).
 // No TMA multicast is used anywhere. Every wait is bounded (see mbar_wait).
 #pragma once
+#include "kernels.cuh"
 #include "sm100.cuh"
 
 namespace sb {
@@ -49,6 +50,11 @@ struct ProductParams {
   double* partials;      // reduce mode: [gridDim.x][2] per-CTA (sum, sum of squares)
   int* err;              // device error word (0 = ok)
   unsigned long long timeout_ns;
+  // Fused finalize (product mode, splits == 1, DP <= 32): when fin.mode != FIN_NONE the epilogue
+  // applies the support correction and the per-mode update of kernels.cu's finalize pass to each
+  // row as soon as its Y is complete, instead of writing Y to `ws`.
+  int fuse;              // 0: write ws; 1: apply `fin` in the epilogue
+  FinalizeArgs fin;
 };
 
 template <int DP, int BN, int STAGES, bool X3, bool REDUCE, int NXB>
@@ -90,6 +96,87 @@ struct ProductCfg {
   static_assert(EPI_COLS % 16 == 0, "epilogue column split");
   static constexpr int LDW = EPI_COLS % 32 == 0 ? 32 : 16;  // tcgen05.ld/st width used
 };
+
+// The finalize pass of kernels.cu for one row j whose Y (DP values) is in registers: support
+// correction with L = <X_j, F_i> (fp32) and the FIN_SALSA / FIN_GRAD / FIN_STORE update.
+template <int DP>
+__device__ __forceinline__ void epilogue_finalize(const FinalizeArgs& a, int64_t j, const float* y) {
+  float x[DP], cor[DP];
+  const float4* xr = reinterpret_cast<const float4*>(a.X + j * DP);
+#pragma unroll
+  for (int c = 0; c < DP / 4; ++c) {
+    const float4 v = xr[c];
+    x[4 * c] = v.x; x[4 * c + 1] = v.y; x[4 * c + 2] = v.z; x[4 * c + 3] = v.w;
+  }
+#pragma unroll
+  for (int c = 0; c < DP; ++c) cor[c] = 0.f;
+  if (a.rowptr) {
+    const int e0 = a.rowptr[j], e1 = a.rowptr[j + 1];
+    for (int e = e0; e < e1; ++e) {
+      const int2 en = a.ent[e];
+      const float4* fr = reinterpret_cast<const float4*>(a.F + (int64_t)en.x * DP);
+      const float4* cr = reinterpret_cast<const float4*>(a.Cm + (int64_t)en.x * DP);
+      float L = 0.f;
+#pragma unroll
+      for (int c = 0; c < DP / 4; ++c) {
+        const float4 f = fr[c];
+        L = fmaf(x[4 * c], f.x, L);
+        L = fmaf(x[4 * c + 1], f.y, L);
+        L = fmaf(x[4 * c + 2], f.z, L);
+        L = fmaf(x[4 * c + 3], f.w, L);
+      }
+      const float val = __int_as_float(en.y);
+      const float coef = (a.mode == FIN_SALSA) ? (val - L + fmaxf(L, 0.f)) : (L - val - fmaxf(L, 0.f));
+#pragma unroll
+      for (int c = 0; c < DP / 4; ++c) {
+        const float4 cv = cr[c];
+        cor[4 * c] = fmaf(coef, cv.x, cor[4 * c]);
+        cor[4 * c + 1] = fmaf(coef, cv.y, cor[4 * c + 1]);
+        cor[4 * c + 2] = fmaf(coef, cv.z, cor[4 * c + 2]);
+        cor[4 * c + 3] = fmaf(coef, cv.w, cor[4 * c + 3]);
+      }
+    }
+  }
+  if (a.mode == FIN_SALSA) {
+    const float mu = a.momentum, one_m_mu = 1.0f - mu, ub = *a.unbias;
+    float4* xw = reinterpret_cast<float4*>(a.X + j * DP);
+    float4* dw = reinterpret_cast<float4*>(a.dX + j * DP);
+#pragma unroll
+    for (int c = 0; c < DP / 4; ++c) {
+      const float4 dx = dw[c];
+      const float dxv[4] = {dx.x, dx.y, dx.z, dx.w};
+      float nx[4], ndx[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int i = 4 * c + u;
+        const float lsq = (x[i] - y[i]) + cor[i];
+        ndx[u] = (lsq - x[i]) * one_m_mu + dxv[u] * mu;
+        nx[u] = x[i] + a.lrate * ndx[u] / ub;
+      }
+      xw[c] = make_float4(nx[0], nx[1], nx[2], nx[3]);
+      dw[c] = make_float4(ndx[0], ndx[1], ndx[2], ndx[3]);
+    }
+  } else if (a.mode == FIN_STORE) {
+    const int64_t orow = a.out_rows ? a.out_rows[j] : j;
+    float* o = a.out + orow * a.ld_out;
+#pragma unroll
+    for (int c = 0; c < DP; ++c)
+      if (c < a.out_d) o[c] = y[c] + cor[c];
+  } else {
+    const int64_t orow = a.out_rows ? a.out_rows[j] : j;
+    float4* o = reinterpret_cast<float4*>(a.out + orow * DP);
+#pragma unroll
+    for (int c = 0; c < DP / 4; ++c) {
+      float4 r = make_float4(a.scale * (y[4 * c] + cor[4 * c]), a.scale * (y[4 * c + 1] + cor[4 * c + 1]),
+                             a.scale * (y[4 * c + 2] + cor[4 * c + 2]), a.scale * (y[4 * c + 3] + cor[4 * c + 3]));
+      if (a.accumulate) {
+        const float4 old = o[c];
+        r.x += old.x; r.y += old.y; r.z += old.z; r.w += old.w;
+      }
+      o[c] = r;
+    }
+  }
+}
 
 template <int DP, int BN, int STAGES, bool X3, bool REDUCE, int NXB>
 __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>::THREADS, 1)
@@ -430,6 +517,23 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>::T
                        p.timeout_ns)) { ok = false; break; }
         tc_fence_after();
         const int row = tile * Cfg::TM + row_in_tile;
+        if constexpr (DP <= 32) {
+          if (p.fuse) {
+            // warps of half 0 own full rows: read all of Y, release the accumulator, finalize
+            float y[DP];
+            if (half == 0) {
+#pragma unroll
+              for (int col = 0; col < DP; col += 16) {
+                tmem_ld16(tbase + lane_addr + Cfg::TMEM_Y + yb * DP + col, y + col);
+                tmem_ld_wait_regs16(y + col);
+              }
+            }
+            tc_fence_before();
+            mbar_arrive(&y_empty[yb]);
+            if (half == 0 && row < p.M) epilogue_finalize<DP>(p.fin, row, y);
+            continue;
+          }
+        }
         float* out = p.ws + ((size_t)split * p.M + (size_t)(row < p.M ? row : 0)) * DP;
         // the two warps of a quadrant share the 16-column pieces of Y
 #pragma unroll 1

@@ -85,6 +85,11 @@ class SalsaState:
         self.unbias = torch.empty(self.nb, dtype=torch.float32, device=dev)
         self.unbias_host = torch.empty(self.nb, dtype=torch.float32).pin_memory() \
             if torch.cuda.is_available() else None
+        self.use_graph = True
+        self.graph = None
+        self.eager_done = False
+        self.perm_r = torch.empty(m, dtype=torch.int64, device=dev)
+        self.perm_c = torch.empty(n, dtype=torch.int64, device=dev)
         L = _native.lib()
         self.ws_b = ops._ws(dev, L.sumac_salsa_update_workspace_bytes(
             n, self.dir_b.block_size, self.d, self.prec), "salsa_b")
@@ -92,11 +97,36 @@ class SalsaState:
             m, self.dir_a.block_size, self.d, self.prec), "salsa_a")
 
     def iteration(self, it: int, perm_r: Tensor, perm_c: Tensor) -> None:
+        """One SALSA iteration. The first call runs eagerly; later calls replay a CUDA graph of
+        the whole iteration (CSR rebuilds and 2 x num_blocks block updates) that reads the
+        permutations and unbias factors from static device buffers."""
+        nb = self.nb
+        self.unbias_host.copy_(torch.from_numpy(unbias_values(self.momentum, 1 + (it - 1) * nb, nb)))
+        self.unbias.copy_(self.unbias_host, non_blocking=True)
+        if not self.use_graph:
+            self._body(perm_r, perm_c)
+            return
+        if self.graph is None and self.eager_done:
+            self.perm_r.copy_(perm_r)
+            self.perm_c.copy_(perm_c)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._body(self.perm_r, self.perm_c)
+            self.graph = g
+            g.replay()
+            return
+        if self.graph is None:
+            self._body(perm_r, perm_c)
+            self.eager_done = True
+            return
+        self.perm_r.copy_(perm_r)
+        self.perm_c.copy_(perm_c)
+        self.graph.replay()
+
+    def _body(self, perm_r: Tensor, perm_c: Tensor) -> None:
         nb = self.nb
         self.dir_b.rebuild(perm_r)
         self.dir_a.rebuild(perm_c)
-        self.unbias_host.copy_(torch.from_numpy(unbias_values(self.momentum, 1 + (it - 1) * nb, nb)))
-        self.unbias.copy_(self.unbias_host, non_blocking=True)
         for k in range(nb):
             rows = self.dir_b.block_rows(perm_r, k)
             if rows.numel() > 0:
