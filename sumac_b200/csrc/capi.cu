@@ -31,6 +31,7 @@ int cuda_status(int rc, const char* what) {
   if (rc == -1) return fail(SUMAC_ERR_UNSUPPORTED, "%s: unsupported rank/precision", what);
   if (rc == -5) return fail(SUMAC_ERR_ARG, "%s: bad sizes", what);
   if (rc == -6) return fail(SUMAC_ERR_CUDA, "%s: cuTensorMapEncodeTiled failed", what);
+  if (rc == -7) return fail(SUMAC_ERR_ARG, "%s: operand maxima missing", what);
   if (rc < 0) return fail(SUMAC_ERR_ARG, "%s: error %d", what, rc);
   return fail(SUMAC_ERR_CUDA, "%s: %s", what, cudaGetErrorString((cudaError_t)rc));
 }
@@ -103,9 +104,18 @@ int sumac_relu_product(const float* X, int64_t M, const float* Fhi, const float*
     return fail(SUMAC_ERR_ARG, "relu_product: null pointer");
   if (!aligned16(X) || !aligned16(Fhi) || !aligned16(Cthi) || (ldct & 3))
     return fail(SUMAC_ERR_ARG, "relu_product: operands must be 16-byte aligned");
+  // the TF32 product's fp16 second MMA needs the operand maxima: they go to the 16 bytes that
+  // follow the partial outputs in `partials`
+  unsigned int* stats = nullptr;
+  const int splits_p = product_split_count(M, N, Dp, x3, num_sms_current());
+  if (!x3) {
+    stats = reinterpret_cast<unsigned int*>(partials + (size_t)splits_p * M * Dp);
+    launch_operand_stats(Fhi, N, Dp, Cthi, (int64_t)Dp * ldct, stats,
+                         reinterpret_cast<cudaStream_t>(stream));
+  }
   int rc = launch_relu_product(X, M, Fhi, Flo, Cthi, Ctlo, ldct, N, Dp, x3, partials, dev_err,
                                num_sms_current(), g_timeout_ns,
-                               reinterpret_cast<cudaStream_t>(stream));
+                               reinterpret_cast<cudaStream_t>(stream), nullptr, nullptr, stats);
   return cuda_status(rc, "relu_product");
 }
 int sumac_relu_product_splits(int64_t M, int64_t N, int Dp, int precision) {
@@ -121,6 +131,7 @@ int sumac_num_sms(int device) {
 // ------------------------------------------------------------------------------ relu_bat_c
 struct RbcPlan {
   float *Xp, *Fp, *Flo, *Cp, *Cthi, *Ctlo, *part;
+  unsigned int* stats;
   int64_t ldct;
   size_t bytes;
 };
@@ -136,6 +147,7 @@ static RbcPlan plan_relu_bat_c(void* ws, int64_t M, int64_t N, int Dp, bool x3, 
   p.Cthi = b.take<float>((size_t)Dp * p.ldct);
   p.Ctlo = x3 ? b.take<float>((size_t)Dp * p.ldct) : nullptr;
   p.part = b.take<float>((size_t)(splits > 0 ? splits : 1) * M * Dp);
+  p.stats = b.take<unsigned int>(4);
   p.bytes = b.off + 256;
   return p;
 }
@@ -164,8 +176,9 @@ int sumac_relu_bat_c(const float* A, const float* B, const float* C, int64_t M, 
   else launch_gather_pad(A, D, D, nullptr, N, Dp, p.Fp, nullptr, nullptr, s);
   launch_gather_pad(C, D, D, nullptr, N, Dp, p.Cp, nullptr, nullptr, s);
   launch_transpose_split(p.Cp, N, Dp, p.Cthi, p.Ctlo, p.ldct, s);
+  if (!x3) launch_operand_stats(p.Fp, N, Dp, p.Cthi, (int64_t)Dp * p.ldct, p.stats, s);
   int rc = launch_relu_product(p.Xp, M, p.Fp, p.Flo, p.Cthi, p.Ctlo, p.ldct, N, Dp, x3, p.part,
-                               dev_err, sms, g_timeout_ns, s);
+                               dev_err, sms, g_timeout_ns, s, nullptr, nullptr, p.stats);
   if (rc) return cuda_status(rc, "relu_bat_c");
   FinalizeArgs f{};
   f.mode = FIN_STORE; f.M = M; f.Dp = Dp; f.splits = product_split_count(M, N, Dp, x3, sms);
@@ -224,6 +237,7 @@ int sumac_relu_bat_reduce(const float* A, const float* B, int64_t M, int64_t N, 
 // ------------------------------------------------------------------------------ masked product
 struct MpPlan {
   float *Fhi, *Flo, *Cthi, *Ctlo, *part;
+  unsigned int* stats;
   int64_t ldct;
   size_t bytes;
 };
@@ -237,6 +251,7 @@ static MpPlan plan_masked(void* ws, int64_t M, int64_t N, int Dp, bool x3, int s
   p.Ctlo = x3 ? b.take<float>((size_t)Dp * p.ldct) : nullptr;
   const int splits = product_split_count(M, N, Dp, x3, sms);
   p.part = b.take<float>((size_t)(splits > 0 ? splits : 1) * M * Dp);
+  p.stats = b.take<unsigned int>(4);
   p.bytes = b.off + 256;
   return p;
 }
@@ -263,6 +278,7 @@ int sumac_masked_product(const float* X, const float* F, const float* C, int64_t
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (x3) launch_gather_pad(F, Dp, Dp, nullptr, N, Dp, nullptr, p.Fhi, p.Flo, s);
   launch_transpose_split(C, N, Dp, p.Cthi, p.Ctlo, p.ldct, s);
+  if (!x3) launch_operand_stats(F, N, Dp, p.Cthi, (int64_t)Dp * p.ldct, p.stats, s);
   FinalizeArgs f{};
   f.mode = FIN_STORE; f.M = M; f.Dp = Dp; f.splits = product_split_count(M, N, Dp, x3, sms);
   f.ws = p.part; f.X = const_cast<float*>(X); f.F = F; f.Cm = C;
@@ -270,7 +286,7 @@ int sumac_masked_product(const float* X, const float* F, const float* C, int64_t
   f.out = Y; f.out_d = Dp; f.ld_out = Dp;
   int fused = 0;
   int rc = launch_relu_product(X, M, x3 ? p.Fhi : F, p.Flo, p.Cthi, p.Ctlo, p.ldct, N, Dp, x3,
-                               p.part, dev_err, sms, g_timeout_ns, s, &f, &fused);
+                               p.part, dev_err, sms, g_timeout_ns, s, &f, &fused, p.stats);
   if (rc) return cuda_status(rc, "masked_product");
   if (!fused) launch_finalize(f, s);
   return launched("masked_product");
@@ -297,7 +313,7 @@ static SalsaPlan plan_salsa(void* ws, int64_t M, int64_t b, int d, int Dp, bool 
   const size_t gbytes = (size_t)gram_parts(b) * d * d * sizeof(double);
   const size_t pbytes = salsa_prep_scratch_bytes(b, d);
   p.gram = bp.take<double>(((gbytes > pbytes ? gbytes : pbytes) + 7) / 8);
-  p.counter = bp.take<unsigned int>(64);
+  p.counter = bp.take<unsigned int>(64);  // [0] done-CTA counter, [1..2] operand maxima
   // the split count grows as b shrinks; size for the worst case over b' <= b
   int smax = 1;
   for (int64_t bb = b; bb > 0; bb = bb / 2) {
@@ -336,13 +352,14 @@ int sumac_salsa_block_update(const float* F, int64_t m_fixed, const int64_t* row
     return fail(SUMAC_ERR_WORKSPACE, "salsa_block_update: workspace %zu < %zu", ws_bytes, p.bytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (d <= 32) {
-    cudaMemsetAsync(p.counter, 0, sizeof(unsigned int), s);
+    cudaMemsetAsync(p.counter, 0, 3 * sizeof(unsigned int), s);
     launch_salsa_prep(F, rows, b, d, Dp, p.FI, p.Fhi, p.Flo, p.P, p.Cthi, p.Ctlo, p.ldct, p.gram,
-                      p.counter, dev_err, s);
+                      p.counter, x3 ? nullptr : p.counter + 1, dev_err, s);
   } else {
     launch_gather_pad(F, Dp, Dp, rows, b, Dp, p.FI, p.Fhi, p.Flo, s);
     launch_gram(p.FI, b, d, Dp, p.gram, s);
     launch_solve(p.FI, b, d, Dp, p.gram, gram_parts(b), p.P, p.Cthi, p.Ctlo, p.ldct, dev_err, s);
+    if (!x3) launch_operand_stats(p.FI, b, Dp, p.Cthi, (int64_t)Dp * p.ldct, p.counter + 1, s);
   }
   FinalizeArgs f{};
   f.mode = FIN_SALSA; f.M = M; f.Dp = Dp; f.splits = product_split_count(M, b, Dp, x3, sms);
@@ -351,7 +368,8 @@ int sumac_salsa_block_update(const float* F, int64_t m_fixed, const int64_t* row
   f.momentum = momentum; f.lrate = lrate; f.unbias = unbias;
   int fused = 0;
   int rc = launch_relu_product(X, M, x3 ? p.Fhi : p.FI, p.Flo, p.Cthi, p.Ctlo, p.ldct, b, Dp, x3,
-                               p.part, dev_err, sms, g_timeout_ns, s, nullptr, &fused);
+                               p.part, dev_err, sms, g_timeout_ns, s, nullptr, &fused,
+                               p.counter + 1);
   if (rc) return cuda_status(rc, "salsa_block_update");
   if (!fused) launch_finalize(f, s);
   return launched("salsa_block_update");
@@ -382,6 +400,7 @@ int sumac_block_csr_build(const int64_t* perm, int64_t m_fixed, int num_blocks,
 // ------------------------------------------------------------------------------ GD block gradient
 struct GdPlan {
   float *AI, *AIhi, *AIlo, *AIthi, *AItlo, *Bhi, *Blo, *Bthi, *Btlo, *part;
+  unsigned int* stats;
   int64_t ldb, ldn;
   size_t bytes;
 };
@@ -408,6 +427,7 @@ static GdPlan plan_gd(void* ws, int64_t n, int64_t b, int Dp, bool x3, int sms) 
     if (bb == 1) break;
   }
   p.part = bp.take<float>(need);
+  p.stats = bp.take<unsigned int>(8);
   p.bytes = bp.off + 256;
   return p;
 }
@@ -439,6 +459,7 @@ int sumac_gd_block_grad(const float* A, const float* B, int64_t n, int d, const 
   // pass B: rows j of B, contraction over the b block rows; C = A_I
   launch_gather_pad(A, Dp, Dp, rows, b, Dp, p.AI, p.AIhi, p.AIlo, s);
   launch_transpose_split(p.AI, b, Dp, p.AIthi, p.AItlo, p.ldb, s);
+  if (!x3) launch_operand_stats(p.AI, b, Dp, p.AIthi, (int64_t)Dp * p.ldb, p.stats, s);
   FinalizeArgs f{};
   f.mode = FIN_GRAD; f.M = n; f.Dp = Dp; f.splits = product_split_count(n, b, Dp, x3, sms);
   f.ws = p.part; f.X = const_cast<float*>(B); f.F = p.AI; f.Cm = p.AI;
@@ -446,14 +467,16 @@ int sumac_gd_block_grad(const float* A, const float* B, int64_t n, int d, const 
   f.out = gB; f.scale = 2.f; f.accumulate = accumulate;
   int fused = 0;
   int rc = launch_relu_product(B, n, x3 ? p.AIhi : p.AI, p.AIlo, p.AIthi, p.AItlo, p.ldb, b, Dp,
-                               x3, p.part, dev_err, sms, g_timeout_ns, s, nullptr, &fused);
+                               x3, p.part, dev_err, sms, g_timeout_ns, s, nullptr, &fused,
+                               p.stats);
   if (rc) return cuda_status(rc, "gd_block_grad (B pass)");
   if (!fused) launch_finalize(f, s);
   // pass A: rows i of A_I, contraction over all n rows of B; C = B
   if (x3) launch_gather_pad(B, Dp, Dp, nullptr, n, Dp, nullptr, p.Bhi, p.Blo, s);
   launch_transpose_split(B, n, Dp, p.Bthi, p.Btlo, p.ldn, s);
+  if (!x3) launch_operand_stats(B, n, Dp, p.Bthi, (int64_t)Dp * p.ldn, p.stats + 4, s);
   rc = launch_relu_product(p.AI, b, x3 ? p.Bhi : B, p.Blo, p.Bthi, p.Btlo, p.ldn, n, Dp, x3,
-                           p.part, dev_err, sms, g_timeout_ns, s);
+                           p.part, dev_err, sms, g_timeout_ns, s, nullptr, nullptr, p.stats + 4);
   if (rc) return cuda_status(rc, "gd_block_grad (A pass)");
   FinalizeArgs g{};
   g.mode = FIN_GRAD; g.M = b; g.Dp = Dp; g.splits = product_split_count(b, n, Dp, x3, sms);

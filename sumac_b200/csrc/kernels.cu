@@ -309,7 +309,8 @@ __global__ void salsa_gram_kernel(const float* __restrict__ Ffix, const int64_t*
                                   int64_t b, int d, int Dp, float* __restrict__ FI,
                                   float* __restrict__ Fhi, float* __restrict__ Flo,
                                   double* __restrict__ parts, unsigned int* counter,
-                                  double* __restrict__ LU, int* __restrict__ piv, int* err) {
+                                  double* __restrict__ LU, int* __restrict__ piv,
+                                  unsigned int* stats, int* err) {
   extern __shared__ float srow[];  // [PREP_ROWS][Dp]
   __shared__ double sG[D * D];
   __shared__ bool last;
@@ -328,6 +329,11 @@ __global__ void salsa_gram_kernel(const float* __restrict__ Ffix, const int64_t*
     }
   }
   __syncthreads();
+  if (stats && threadIdx.x < nr) {
+    float n2 = 0.f;
+    for (int c = 0; c < Dp; ++c) n2 = fmaf(srow[threadIdx.x * Dp + c], srow[threadIdx.x * Dp + c], n2);
+    atomicMax(&stats[0], __float_as_uint(sqrtf(n2)));
+  }
   const int dd = d * d;
   for (int e = threadIdx.x; e < dd; e += blockDim.x) {
     const int i = e / d, j = e - i * d;
@@ -360,7 +366,8 @@ __global__ void __launch_bounds__(128) salsa_solve_kernel(const float* __restric
                                                           const int* __restrict__ piv_g,
                                                           float* __restrict__ P,
                                                           float* __restrict__ Cthi,
-                                                          float* __restrict__ Ctlo, int64_t ldct) {
+                                                          float* __restrict__ Ctlo, int64_t ldct,
+                                                          unsigned int* stats) {
   __shared__ double sLU[D][D + 1];
   __shared__ int piv[D];
   for (int e = threadIdx.x; e < D * D; e += blockDim.x) sLU[e / D][e % D] = LU[e];
@@ -392,9 +399,11 @@ __global__ void __launch_bounds__(128) salsa_solve_kernel(const float* __restric
     for (int j = i + 1; j < D; ++j) s -= sLU[i][j] * x[j];
     x[i] = s / sLU[i][i];
   }
+  float amax = 0.f;
 #pragma unroll
   for (int c = 0; c < D; ++c) {
     const float v = c < d ? (float)x[c] : 0.f;
+    amax = fmaxf(amax, fabsf(v));
     P[r * Dp + c] = v;
     if (Ctlo) {
       const float h = tf32_hi(v);
@@ -404,6 +413,7 @@ __global__ void __launch_bounds__(128) salsa_solve_kernel(const float* __restric
       Cthi[c * ldct + r] = v;
     }
   }
+  if (stats) atomicMax(&stats[1], __float_as_uint(amax));
 }
 
 size_t salsa_prep_scratch_bytes(int64_t b, int d) {
@@ -414,7 +424,8 @@ size_t salsa_prep_scratch_bytes(int64_t b, int d) {
 
 void launch_salsa_prep(const float* Ffix, const int64_t* rows, int64_t b, int d, int Dp, float* FI,
                        float* Fhi, float* Flo, float* P, float* Cthi, float* Ctlo, int64_t ldct,
-                       void* scratch, unsigned int* counter, int* err, cudaStream_t stream) {
+                       void* scratch, unsigned int* counter, unsigned int* stats, int* err,
+                       cudaStream_t stream) {
   const int np = salsa_gram_parts(b);
   const int D = Dp;
   double* parts = reinterpret_cast<double*>(scratch);
@@ -426,13 +437,54 @@ void launch_salsa_prep(const float* Ffix, const int64_t* rows, int64_t b, int d,
   count_launch();
   if (D == 16) {
     salsa_gram_kernel<16><<<np, 256, smem, stream>>>(Ffix, rows, b, d, Dp, FI, Fhi, Flo, parts,
-                                                     counter, LU, piv, err);
-    salsa_solve_kernel<16><<<grid, 128, 0, stream>>>(FI, b, d, Dp, LU, piv, P, Cthi, Ctlo, ldct);
+                                                     counter, LU, piv, stats, err);
+    salsa_solve_kernel<16><<<grid, 128, 0, stream>>>(FI, b, d, Dp, LU, piv, P, Cthi, Ctlo, ldct,
+                                                     stats);
   } else {
     salsa_gram_kernel<32><<<np, 256, smem, stream>>>(Ffix, rows, b, d, Dp, FI, Fhi, Flo, parts,
-                                                     counter, LU, piv, err);
-    salsa_solve_kernel<32><<<grid, 128, 0, stream>>>(FI, b, d, Dp, LU, piv, P, Cthi, Ctlo, ldct);
+                                                     counter, LU, piv, stats, err);
+    salsa_solve_kernel<32><<<grid, 128, 0, stream>>>(FI, b, d, Dp, LU, piv, P, Cthi, Ctlo, ldct,
+                                                     stats);
   }
+}
+
+
+// ============================================================================================
+// operand maxima for the fp16 second MMA: max row norm of F, max |C|
+// ============================================================================================
+__global__ void operand_stats_kernel(const float* __restrict__ F, int64_t N, int Dp,
+                                     const float* __restrict__ C, int64_t nC, unsigned int* stats) {
+  float fm = 0.f, cm = 0.f;
+  for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < N;
+       r += (int64_t)gridDim.x * blockDim.x) {
+    const float4* fr = reinterpret_cast<const float4*>(F + r * Dp);
+    float n2 = 0.f;
+    for (int c = 0; c < Dp / 4; ++c) {
+      const float4 v = fr[c];
+      n2 = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, n2))));
+    }
+    fm = fmaxf(fm, sqrtf(n2));
+  }
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nC;
+       i += (int64_t)gridDim.x * blockDim.x)
+    cm = fmaxf(cm, fabsf(C[i]));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    fm = fmaxf(fm, __shfl_xor_sync(0xffffffffu, fm, o));
+    cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicMax(&stats[0], __float_as_uint(fm));
+    atomicMax(&stats[1], __float_as_uint(cm));
+  }
+}
+
+void launch_operand_stats(const float* F, int64_t N, int Dp, const float* C, int64_t nC,
+                          unsigned int* stats, cudaStream_t stream) {
+  cudaMemsetAsync(stats, 0, 2 * sizeof(unsigned int), stream);
+  count_launch();
+  const int64_t work = N > nC ? N : nC;
+  operand_stats_kernel<<<grid_cap(work, 256, 148 * 4), 256, 0, stream>>>(F, N, Dp, C, nC, stats);
 }
 
 // ============================================================================================

@@ -22,7 +22,12 @@ int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float
                         const float* Cthi, const float* Ctlo, int64_t ldct, int64_t N, int Dp,
                         bool x3, float* ws, int* err, int num_sms, unsigned long long timeout_ns,
                         cudaStream_t stream, const FinalizeArgs* fin = nullptr,
-                        int* fused = nullptr);
+                        int* fused = nullptr, const unsigned int* stats = nullptr);
+// stats[0] = bits of max_r |F[r]| (row norm over Dp), stats[1] = bits of max |C| over nC values
+// (atomicMax on non-negative float bits; the words must be zero beforehand). The TF32 product
+// (fp16 second MMA) reads them to pick exact power-of-two scales.
+void launch_operand_stats(const float* F, int64_t N, int Dp, const float* C, int64_t nC,
+                          unsigned int* stats, cudaStream_t stream);
 // Reduce mode: partials[grid][2] (grid <= num_sms) hold per-CTA (sum ReLU, sum ReLU^2).
 int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float* Flo, int64_t N,
                        int Dp, bool x3, double* partials, int* grid_out, int* err, int num_sms,
@@ -55,9 +60,11 @@ void launch_solve(const float* FI, int64_t b, int d, int Dp, const double* gram_
 // launch (the kernels leave it zero).
 int salsa_gram_parts(int64_t b);
 size_t salsa_prep_scratch_bytes(int64_t b, int d);
+// Also accumulates the operand maxima of the following product into stats[0..1] (zero before).
 void launch_salsa_prep(const float* Ffix, const int64_t* rows, int64_t b, int d, int Dp, float* FI,
                        float* Fhi, float* Flo, float* P, float* Cthi, float* Ctlo, int64_t ldct,
-                       void* scratch, unsigned int* counter, int* err, cudaStream_t stream);
+                       void* scratch, unsigned int* counter, unsigned int* stats, int* err,
+                       cudaStream_t stream);
 
 // ---- finalize: sparse correction + update -------------------------------------------------
 enum FinalizeMode { FIN_STORE = 0, FIN_SALSA = 1, FIN_GRAD = 2 };

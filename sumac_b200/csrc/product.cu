@@ -179,10 +179,12 @@ static CUtensorMapSwizzle row_swizzle(int Dp) {
 int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float* Flo,
                         const float* Cthi, const float* Ctlo, int64_t ldct, int64_t N, int Dp,
                         bool x3, float* ws, int* err, int num_sms, unsigned long long timeout_ns,
-                        cudaStream_t stream, const FinalizeArgs* fin, int* fused) {
+                        cudaStream_t stream, const FinalizeArgs* fin, int* fused,
+                        const unsigned int* stats) {
   ProdCfgRt c = product_cfg(Dp, x3);
   if (!c.ok) return -1;
   if (M <= 0 || N <= 0 || M >= INT32_MAX || N >= INT32_MAX) return -5;
+  if (!x3 && !stats) return -7;  // the fp16 second MMA needs the operand maxima
   const uint32_t box_k = Dp * 4 <= 128 ? Dp : 32;
   CUtensorMap mx, mfh, mfl, mch, mcl;
   const CUtensorMapSwizzle sw = row_swizzle(Dp);
@@ -199,6 +201,8 @@ int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float
   p.partials = nullptr;
   p.err = err;
   p.timeout_ns = timeout_ns;
+  p.Xg = X;
+  p.stats = stats;
   p.fuse = (fin != nullptr && p.splits == 1 && Dp <= 32) ? 1 : 0;
   if (p.fuse) p.fin = *fin;
   else memset(&p.fin, 0, sizeof(p.fin));
@@ -225,6 +229,8 @@ int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float*
   p.N = (int)N;
   plan_splits(M, N, c.bn, num_sms, &p.splits, &p.chunks_per_split, &p.n_chunks, &p.n_tiles);
   p.ws = nullptr;
+  p.Xg = X;
+  p.stats = nullptr;
   p.fuse = 0;
   memset(&p.fin, 0, sizeof(p.fin));
   p.partials = partials;

@@ -35,6 +35,8 @@
 // No TMA multicast is used anywhere. Every wait is bounded (see mbar_wait).
 #pragma once
 #include "kernels.cuh"
+#include <cuda_fp16.h>
+
 #include "sm100.cuh"
 
 namespace sb {
@@ -55,6 +57,11 @@ struct ProductParams {
   // row as soon as its Y is complete, instead of writing Y to `ws`.
   int fuse;              // 0: write ws; 1: apply `fin` in the epilogue
   FinalizeArgs fin;
+  // TF32 product mode: the second MMA runs in fp16 (kind::f16, same 10-bit mantissa as tf32,
+  // K = 16 per instruction). stats[0] = bits of max_i |F_i| (row norm), stats[1] = bits of
+  // max |C|; R rows and C are scaled by exact powers of two so that no fp16 value overflows.
+  const float* Xg;                // X in global memory (row norms for the R scale)
+  const unsigned int* stats;
 };
 
 template <int DP, int BN, int STAGES, bool X3, bool REDUCE, int NXB>
@@ -71,10 +78,13 @@ struct ProductCfg {
   static constexpr int F_BYTES = BN * DP * 4;
   static constexpr int C_BYTES = REDUCE ? 0 : DP * BN * 4;
   static constexpr int NPREC = X3 ? 2 : 1;
-  static constexpr int STAGE_BYTES = NPREC * (F_BYTES + C_BYTES);
+  static constexpr int STAGE_BYTES = NPREC * (F_BYTES + C_BYTES);   // bytes the TMA fills
+  static constexpr bool H16 = !X3 && !REDUCE;                     // fp16 second MMA
+  static constexpr int C16_BYTES = H16 ? DP * BN * 2 : 0;         // fp16 copy of the C chunk
+  static constexpr int STAGE_ALLOC = STAGE_BYTES + C16_BYTES;
   static constexpr int XBUF_BYTES = NPREC * X_BYTES;      // one X buffer (hi [, lo])
   static constexpr int X_TOTAL = NXB * XBUF_BYTES;
-  static constexpr int SMEM_DATA = X_TOTAL + STAGES * STAGE_BYTES;
+  static constexpr int SMEM_DATA = X_TOTAL + STAGES * STAGE_ALLOC;
   static constexpr int SMEM_BYTES_RAW = SMEM_DATA + 1024 /*barriers*/ + 1024 /*align slack*/;
   // at least 120 KB so that only one CTA (and one 512-column TMEM allocation) lives on an SM
   static constexpr int SMEM_BYTES = SMEM_BYTES_RAW < 122880 ? 122880 : SMEM_BYTES_RAW;
@@ -89,9 +99,12 @@ struct ProductCfg {
   static_assert(REDUCE || STAGES >= 2, "product mode needs two stages (MMA2 lags MMA1)");
   static constexpr uint32_t IDESC1 = umma_idesc_tf32(TM, BN);
   static constexpr uint32_t IDESC2 = umma_idesc_tf32(TM, DP);
+  // kind::f16: f32 accumulate, A and B f16, both K-major
+  static constexpr uint32_t IDESC2_F16 =
+      (1u << 4) | ((uint32_t)(DP >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
   static constexpr int EPI_WARPS = 8;                     // two per TMEM lane quadrant
   static constexpr int EPI_THREADS = 32 * EPI_WARPS;
-  static constexpr int THREADS = 64 + EPI_THREADS + (X3 ? 32 : 0);
+  static constexpr int THREADS = 64 + EPI_THREADS + ((X3 || H16) ? 32 : 0);
   static constexpr int EPI_COLS = BN / 2;                 // S columns per epilogue warp
   static_assert(EPI_COLS % 16 == 0, "epilogue column split");
   static constexpr int LDW = EPI_COLS % 32 == 0 ? 32 : 16;  // tcgen05.ld/st width used
@@ -191,7 +204,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>::T
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* sX = smem;                                   // [NXB][NPREC][X_BYTES]
-  uint8_t* sStage = smem + Cfg::X_TOTAL;                // [STAGES][STAGE_BYTES]
+  uint8_t* sStage = smem + Cfg::X_TOTAL;                // [STAGES][STAGE_ALLOC]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::SMEM_DATA);
   uint64_t* full = bars;                    // [STAGES]
   uint64_t* empty = full + STAGES;          // [STAGES]
@@ -203,7 +216,8 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>::T
   uint64_t* y_full = x_ready + 2;           // [2]
   uint64_t* y_empty = y_full + 2;           // [2]
   uint64_t* drain = y_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* c16_ready = drain + 1;          // [STAGES] fp16 C chunk converted (H16)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(c16_ready + STAGES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   double* red = reinterpret_cast<double*>(smem + Cfg::SMEM_DATA + 512);  // [EPI_WARPS][2]
 
@@ -228,6 +242,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>::T
       mbar_init(&y_empty[b], Cfg::EPI_THREADS);
     }
     mbar_init(drain, 1);
+    for (int s = 0; s < STAGES; ++s) mbar_init(&c16_ready[s], 32);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -281,7 +296,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>::T
           // a stage is free once the empty barrier completed its previous round
           if (round > 0 && !mbar_wait(&empty[stage], (round - 1) & 1, abort_flag, p.err,
                                       DEV_TIMEOUT_EMPTY, p.timeout_ns)) { ok = false; break; }
-          uint8_t* st = sStage + stage * Cfg::STAGE_BYTES;
+          uint8_t* st = sStage + stage * Cfg::STAGE_ALLOC;
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
 #pragma unroll
           for (int h = 0; h < Cfg::NPREC; ++h) {
@@ -324,7 +339,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>::T
       // FIFO of chunks whose second MMA is still to be issued (product mode)
       struct Pend {
         int stage, buf, t;
-        uint32_t use;
+        uint32_t use, sphase;
         bool first, last;
       };
       Pend q[NBUF];
@@ -337,11 +352,29 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>::T
           if (!mbar_wait(&y_empty[yb], ((e.t >> 1) - 1) & 1, abort_flag, p.err, DEV_TIMEOUT_Y,
                          p.timeout_ns)) return false;
         }
+        if (Cfg::H16 && !mbar_wait(&c16_ready[e.stage], e.sphase, abort_flag, p.err,
+                                   DEV_TIMEOUT_FULL, p.timeout_ns)) return false;
         tc_fence_after();
-        const uint32_t cbase = sSt_addr + e.stage * Cfg::STAGE_BYTES + Cfg::NPREC * Cfg::F_BYTES;
+        const uint32_t cbase = sSt_addr + e.stage * Cfg::STAGE_ALLOC + Cfg::NPREC * Cfg::F_BYTES;
         const uint32_t s_hi = tbase + e.buf * BN;
         const uint32_t s_lo = tbase + Cfg::TMEM_S_LO + e.buf * BN;
         const uint32_t ytm = tbase + Cfg::TMEM_Y + yb * DP;
+        if constexpr (Cfg::H16) {
+          // R packed as fp16 pairs: warp half h holds k in [h*EPI_COLS, (h+1)*EPI_COLS) in its
+          // own first EPI_COLS/2 columns; C in fp16, 64-element 128 B swizzled sub-tiles
+          const uint32_t c16 = sSt_addr + e.stage * Cfg::STAGE_ALLOC + Cfg::STAGE_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const int hh = (16 * kk) / Cfg::EPI_COLS;
+            const uint32_t acol = hh * Cfg::EPI_COLS + (16 * kk - hh * Cfg::EPI_COLS) / 2;
+            const uint32_t off = (kk >> 2) * (DP * 128) + (kk & 3) * 32;
+            const uint64_t bd = umma_sdesc(c16 + off, 16, 1024, UMMA_SW128);
+            mma_f16_ts(ytm, s_hi + acol, bd, Cfg::IDESC2_F16, (e.first && kk == 0) ? 0u : 1u);
+          }
+          mma_commit(&empty[e.stage]);
+          if (e.last) mma_commit(&y_full[yb]);
+          return true;
+        }
 #pragma unroll
         for (int kk = 0; kk < BN / 8; ++kk) {
           const uint32_t off = (kk >> 2) * (DP * 128) + (kk & 3) * 32;
@@ -384,7 +417,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>::T
                            DEV_TIMEOUT_RREADY, p.timeout_ns)) { ok = false; break; }
           }
           tc_fence_after();
-          const uint32_t fbase = sSt_addr + stage * Cfg::STAGE_BYTES;
+          const uint32_t fbase = sSt_addr + stage * Cfg::STAGE_ALLOC;
           const uint32_t s_tm = tbase + buf * BN;
 #pragma unroll
           for (int kk = 0; kk < DP / 8; ++kk) {
@@ -410,7 +443,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>::T
           if (REDUCE) mma_commit(&empty[stage]);
           if (c == c1 - 1) mma_commit(&x_empty[xb]);  // last use of this X tile
           if (!REDUCE) {
-            q[(qh + qn) % NBUF] = Pend{stage, buf, t, buf_uses[buf], c == c0, c == c1 - 1};
+            q[(qh + qn) % NBUF] = Pend{stage, buf, t, buf_uses[buf], phase, c == c0, c == c1 - 1};
             ++qn;
             if (qn > Cfg::LAG) {  // keep LAG chunks of lookahead
               if (!issue_second(q[qh])) { ok = false; break; }
@@ -446,10 +479,40 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>::T
     double acc_s = 0.0, acc_s2 = 0.0;
     int t = 0;
     bool ok = true;
+    // fp16 second MMA: C is scaled by 2^ec (fixed per launch), row j of R by 2^er(j)
+    int ec = 0;
+    float fmax = 0.f;
+    if constexpr (Cfg::H16) {
+      fmax = __uint_as_float(p.stats[0]);
+      const float cmax = __uint_as_float(p.stats[1]);
+      int ex = 0;
+      if (cmax > 0.f) frexpf(cmax, &ex);
+      ec = 14 - ex;
+    }
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++t) {
       const int tile = item / p.splits, split = item % p.splits;
       const int c0 = split * p.chunks_per_split;
       const int c1 = min(p.n_chunks, c0 + p.chunks_per_split);
+      int er = 0;
+      float rscale = 1.f;
+      if constexpr (Cfg::H16) {
+        // |S_ji| <= |x_j| max_i |F_i|: scale the row so that |R| < 2^15
+        const int row = tile * Cfg::TM + row_in_tile;
+        if (row < p.M) {
+          const float4* xr = reinterpret_cast<const float4*>(p.Xg + (size_t)row * DP);
+          float n2 = 0.f;
+#pragma unroll
+          for (int c = 0; c < DP / 4; ++c) {
+            const float4 xv = xr[c];
+            n2 = fmaf(xv.x, xv.x, fmaf(xv.y, xv.y, fmaf(xv.z, xv.z, fmaf(xv.w, xv.w, n2))));
+          }
+          const float bound = sqrtf(n2) * fmax * 1.001f;
+          int ex = 0;
+          if (bound > 0.f) frexpf(bound, &ex);
+          er = 14 - ex;
+          rscale = ldexpf(1.f, er);
+        }
+      }
       for (int c = c0; c < c1; ++c) {
         const int buf = gchunk % NBUF;
         if (!mbar_wait(&s_full[buf], buf_uses[buf] & 1, abort_flag, p.err, DEV_TIMEOUT_SFULL,
@@ -497,6 +560,17 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>::T
             }
           }
           tmem_st_wait();
+        } else if constexpr (Cfg::H16) {
+          // pack R (scaled) as fp16 pairs (even k in the low half) into this warp's own columns
+          uint32_t pk[Cfg::EPI_COLS / 2];
+#pragma unroll
+          for (int i = 0; i < Cfg::EPI_COLS / 2; ++i) {
+            const __half2 h2 = __floats2half2_rn(v[2 * i] * rscale, v[2 * i + 1] * rscale);
+            pk[i] = *reinterpret_cast<const uint32_t*>(&h2);
+          }
+          if constexpr (Cfg::EPI_COLS / 2 == 32) tmem_st32(s_tm, reinterpret_cast<const float*>(pk));
+          else tmem_st16(s_tm, reinterpret_cast<const float*>(pk));
+          tmem_st_wait();
         } else {
 #pragma unroll
           for (int col = 0; col < Cfg::EPI_COLS; col += Cfg::LDW) {
@@ -527,6 +601,11 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>::T
                 tmem_ld16(tbase + lane_addr + Cfg::TMEM_Y + yb * DP + col, y + col);
                 tmem_ld_wait_regs16(y + col);
               }
+              if constexpr (Cfg::H16) {
+                const float inv = ldexpf(1.f, -(er + ec));
+#pragma unroll
+                for (int i = 0; i < DP; ++i) y[i] *= inv;
+              }
             }
             tc_fence_before();
             mbar_arrive(&y_empty[yb]);
@@ -541,6 +620,11 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>::T
           float y[16];
           tmem_ld16(tbase + lane_addr + Cfg::TMEM_Y + yb * DP + col, y);
           tmem_ld_wait_regs16(y);
+          if constexpr (Cfg::H16) {
+            const float inv = ldexpf(1.f, -(er + ec));
+#pragma unroll
+            for (int i = 0; i < 16; ++i) y[i] *= inv;
+          }
           if (row < p.M) {
             float4* o4 = reinterpret_cast<float4*>(out + col);
 #pragma unroll
@@ -569,6 +653,50 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>::T
         p.partials[2 * blockIdx.x + 0] = a;
         p.partials[2 * blockIdx.x + 1] = b;
       }
+    }
+  } else if (Cfg::H16) {
+    // ------------------------------------------------------------------ C converter (warp 10)
+    // fp32 C chunk (32-float SW128 sub-tiles) -> fp16, scaled by 2^ec (64-element SW128 sub-tiles)
+    const float cmax = __uint_as_float(p.stats[1]);
+    int ex = 0;
+    if (cmax > 0.f) frexpf(cmax, &ex);
+    const float cscale = ldexpf(1.f, 14 - ex);
+    uint32_t g = 0;
+    for (int item = blockIdx.x; item < n_items; item += gridDim.x) {
+      const int split = item % p.splits;
+      const int c0 = split * p.chunks_per_split;
+      const int c1 = min(p.n_chunks, c0 + p.chunks_per_split);
+      bool ok = true;
+      for (int c = c0; c < c1; ++c, ++g) {
+        const int stage = g % STAGES;
+        const uint32_t round = g / STAGES;
+        if (!mbar_wait(&full[stage], round & 1, abort_flag, p.err, DEV_TIMEOUT_FULL, p.timeout_ns)) {
+          ok = false;
+          break;
+        }
+        const uint8_t* src = sStage + stage * Cfg::STAGE_ALLOC + Cfg::F_BYTES;
+        uint8_t* dst = sStage + stage * Cfg::STAGE_ALLOC + Cfg::STAGE_BYTES;
+        constexpr int UNITS = (BN / 64) * DP * 8;  // 16-byte fp16 units
+        for (int uidx = lane; uidx < UNITS; uidx += 32) {
+          const int u = uidx & 7;
+          const int r = (uidx >> 3) % DP;
+          const int s16 = (uidx >> 3) / DP;
+          const int k0 = 64 * s16 + 8 * u;
+          const int s32 = k0 >> 5, v0 = (k0 & 31) >> 2;
+          const uint8_t* rowp = src + s32 * (DP * 128) + r * 128;
+          const float4 a = *reinterpret_cast<const float4*>(rowp + ((v0 ^ (r & 7)) << 4));
+          const float4 b = *reinterpret_cast<const float4*>(rowp + (((v0 + 1) ^ (r & 7)) << 4));
+          __half2 h[4] = {__floats2half2_rn(a.x * cscale, a.y * cscale),
+                          __floats2half2_rn(a.z * cscale, a.w * cscale),
+                          __floats2half2_rn(b.x * cscale, b.y * cscale),
+                          __floats2half2_rn(b.z * cscale, b.w * cscale)};
+          *reinterpret_cast<uint4*>(dst + s16 * (DP * 128) + r * 128 + ((u ^ (r & 7)) << 4)) =
+              *reinterpret_cast<const uint4*>(h);
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&c16_ready[stage]);
+      }
+      if (!ok) break;
     }
   } else if (X3) {
     // ------------------------------------------------------------------ X splitter (warp 10)
