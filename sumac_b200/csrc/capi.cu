@@ -115,7 +115,7 @@ int sumac_relu_product(const float* X, int64_t M, const float* Fhi, const float*
   }
   int rc = launch_relu_product(X, M, Fhi, Flo, Cthi, Ctlo, ldct, N, Dp, x3, partials, dev_err,
                                num_sms_current(), g_timeout_ns,
-                               reinterpret_cast<cudaStream_t>(stream), nullptr, nullptr, stats);
+                               reinterpret_cast<cudaStream_t>(stream), stats);
   return cuda_status(rc, "relu_product");
 }
 int sumac_relu_product_splits(int64_t M, int64_t N, int Dp, int precision) {
@@ -178,7 +178,7 @@ int sumac_relu_bat_c(const float* A, const float* B, const float* C, int64_t M, 
   launch_transpose_split(p.Cp, N, Dp, p.Cthi, p.Ctlo, p.ldct, s);
   if (!x3) launch_operand_stats(p.Fp, N, Dp, p.Cthi, (int64_t)Dp * p.ldct, p.stats, s);
   int rc = launch_relu_product(p.Xp, M, p.Fp, p.Flo, p.Cthi, p.Ctlo, p.ldct, N, Dp, x3, p.part,
-                               dev_err, sms, g_timeout_ns, s, nullptr, nullptr, p.stats);
+                               dev_err, sms, g_timeout_ns, s, p.stats);
   if (rc) return cuda_status(rc, "relu_bat_c");
   FinalizeArgs f{};
   f.mode = FIN_STORE; f.M = M; f.Dp = Dp; f.splits = product_split_count(M, N, Dp, x3, sms);
@@ -284,11 +284,10 @@ int sumac_masked_product(const float* X, const float* F, const float* C, int64_t
   f.ws = p.part; f.X = const_cast<float*>(X); f.F = F; f.Cm = C;
   f.rowptr = rowptr; f.ent = reinterpret_cast<const int2*>(ent);
   f.out = Y; f.out_d = Dp; f.ld_out = Dp;
-  int fused = 0;
   int rc = launch_relu_product(X, M, x3 ? p.Fhi : F, p.Flo, p.Cthi, p.Ctlo, p.ldct, N, Dp, x3,
-                               p.part, dev_err, sms, g_timeout_ns, s, &f, &fused, p.stats);
+                               p.part, dev_err, sms, g_timeout_ns, s, p.stats);
   if (rc) return cuda_status(rc, "masked_product");
-  if (!fused) launch_finalize(f, s);
+  launch_finalize(f, s);
   return launched("masked_product");
 }
 
@@ -366,12 +365,10 @@ int sumac_salsa_block_update(const float* F, int64_t m_fixed, const int64_t* row
   f.ws = p.part; f.X = X; f.dX = dX; f.F = p.FI; f.Cm = p.P;
   f.rowptr = rowptr; f.ent = reinterpret_cast<const int2*>(ent);
   f.momentum = momentum; f.lrate = lrate; f.unbias = unbias;
-  int fused = 0;
   int rc = launch_relu_product(X, M, x3 ? p.Fhi : p.FI, p.Flo, p.Cthi, p.Ctlo, p.ldct, b, Dp, x3,
-                               p.part, dev_err, sms, g_timeout_ns, s, nullptr, &fused,
-                               p.counter + 1);
+                               p.part, dev_err, sms, g_timeout_ns, s, p.counter + 1);
   if (rc) return cuda_status(rc, "salsa_block_update");
-  if (!fused) launch_finalize(f, s);
+  launch_finalize(f, s);
   return launched("salsa_block_update");
 }
 
@@ -465,18 +462,16 @@ int sumac_gd_block_grad(const float* A, const float* B, int64_t n, int d, const 
   f.ws = p.part; f.X = const_cast<float*>(B); f.F = p.AI; f.Cm = p.AI;
   f.rowptr = rowptr_b; f.ent = reinterpret_cast<const int2*>(ent_b);
   f.out = gB; f.scale = 2.f; f.accumulate = accumulate;
-  int fused = 0;
   int rc = launch_relu_product(B, n, x3 ? p.AIhi : p.AI, p.AIlo, p.AIthi, p.AItlo, p.ldb, b, Dp,
-                               x3, p.part, dev_err, sms, g_timeout_ns, s, nullptr, &fused,
-                               p.stats);
+                               x3, p.part, dev_err, sms, g_timeout_ns, s, p.stats);
   if (rc) return cuda_status(rc, "gd_block_grad (B pass)");
-  if (!fused) launch_finalize(f, s);
+  launch_finalize(f, s);
   // pass A: rows i of A_I, contraction over all n rows of B; C = B
   if (x3) launch_gather_pad(B, Dp, Dp, nullptr, n, Dp, nullptr, p.Bhi, p.Blo, s);
   launch_transpose_split(B, n, Dp, p.Bthi, p.Btlo, p.ldn, s);
   if (!x3) launch_operand_stats(B, n, Dp, p.Bthi, (int64_t)Dp * p.ldn, p.stats + 4, s);
   rc = launch_relu_product(p.AI, b, x3 ? p.Bhi : B, p.Blo, p.Bthi, p.Btlo, p.ldn, n, Dp, x3,
-                           p.part, dev_err, sms, g_timeout_ns, s, nullptr, nullptr, p.stats + 4);
+                           p.part, dev_err, sms, g_timeout_ns, s, p.stats + 4);
   if (rc) return cuda_status(rc, "gd_block_grad (A pass)");
   FinalizeArgs g{};
   g.mode = FIN_GRAD; g.M = b; g.Dp = Dp; g.splits = product_split_count(b, n, Dp, x3, sms);

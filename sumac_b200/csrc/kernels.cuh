@@ -15,14 +15,10 @@ long long launch_count();
 // X [M][Dp], F{hi,lo} [N][Dp], Ct{hi,lo} [Dp][ldct] (row-major, 16-byte aligned rows).
 // Writes ws[splits][M][Dp] partial products (splits = product_split_count(...)). Returns 0 or a
 // cudaError_t value; -1 for an unsupported (Dp, x3) combination, -5 bad sizes, -6 tensor map.
-struct FinalizeArgs;
-// With fin != nullptr and a single split (product_split_count == 1) and Dp <= 32, the epilogue
-// applies the finalize pass itself and ws is not written; returns 1 in *fused in that case.
 int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float* Flo,
                         const float* Cthi, const float* Ctlo, int64_t ldct, int64_t N, int Dp,
                         bool x3, float* ws, int* err, int num_sms, unsigned long long timeout_ns,
-                        cudaStream_t stream, const FinalizeArgs* fin = nullptr,
-                        int* fused = nullptr, const unsigned int* stats = nullptr);
+                        cudaStream_t stream, const unsigned int* stats);
 // stats[0] = bits of max_r |F[r]| (row norm over Dp), stats[1] = bits of max |C| over nC values
 // (atomicMax on non-negative float bits; the words must be zero beforehand). The TF32 product
 // (fp16 second MMA) reads them to pick exact power-of-two scales.

@@ -42,22 +42,24 @@ static bool make_map(CUtensorMap* m, const float* base, uint64_t inner, uint64_t
 }
 
 struct ProdCfgRt {
-  int bn, stages, nxb;
+  int bn, stages, g;  // chunk rows, pipeline stages, row tiles per group
   bool ok;
 };
 
+// Per (Dp, precision): the TMEM budget is NBUF * BN (x2 for 3xTF32) S columns plus G * Dp Y
+// columns <= 512; shared memory holds G X slots and the stages.
 static ProdCfgRt product_cfg(int Dp, bool x3) {
   if (!x3) {
     switch (Dp) {
-      case 16: return {128, 6, 2, true};
-      case 32: return {128, 4, 2, true};
+      case 16: return {128, 4, 8, true};
+      case 32: return {128, 3, 4, true};
       case 64: return {128, 2, 2, true};
       case 128: return {64, 2, 1, true};
     }
   } else {
     switch (Dp) {
-      case 16: return {64, 6, 2, true};
-      case 32: return {64, 4, 2, true};
+      case 16: return {64, 4, 8, true};
+      case 32: return {64, 2, 4, true};
       case 64: return {64, 2, 1, true};
     }
   }
@@ -67,17 +69,17 @@ static ProdCfgRt product_cfg(int Dp, bool x3) {
 static ProdCfgRt reduce_cfg(int Dp, bool x3) {
   if (!x3) {
     switch (Dp) {
-      case 16: return {128, 6, 2, true};
-      case 32: return {128, 4, 2, true};
-      case 64: return {128, 3, 2, true};
+      case 16: return {128, 6, 8, true};
+      case 32: return {128, 4, 8, true};
+      case 64: return {128, 3, 4, true};
       case 128: return {64, 2, 2, true};
       case 256: return {32, 2, 1, true};
     }
   } else {
     switch (Dp) {
-      case 16: return {128, 4, 2, true};
-      case 32: return {128, 3, 2, true};
-      case 64: return {64, 3, 1, true};
+      case 16: return {128, 4, 8, true};
+      case 32: return {128, 3, 4, true};
+      case 64: return {64, 3, 2, true};
       case 128: return {32, 2, 1, true};
     }
   }
@@ -87,41 +89,47 @@ static ProdCfgRt reduce_cfg(int Dp, bool x3) {
 bool product_supported(int Dp, bool x3) { return product_cfg(Dp, x3).ok; }
 bool reduce_supported(int Dp, bool x3) { return reduce_cfg(Dp, x3).ok; }
 
-// Split-K: when there are fewer row tiles than SMs, split the chunk range so that every SM gets
-// work, keeping at least ~4 chunks per split and no empty split.
-static void plan_splits(int64_t M, int64_t N, int bn, int num_sms, int* splits, int* cps,
-                        int* n_chunks, int* n_tiles) {
+// Work plan. With fewer row tiles than SMs: one tile per group and split-K over the chunk range
+// so that every SM gets work (at least ~4 chunks per split, no empty split). Otherwise: no
+// split, and the tiles are cut into balanced contiguous groups of at most G tiles, as many
+// groups as fill whole rounds of the persistent grid.
+static void plan_work(int64_t M, int64_t N, int bn, int G, int num_sms, ProductParams* p) {
   const int64_t tiles = (M + 127) / 128;
   const int64_t nc = (N + bn - 1) / bn;
-  int64_t s = 1;
+  int64_t s = 1, groups = tiles;
   if (tiles < num_sms) {
     s = (num_sms + tiles - 1) / tiles;
     int64_t max_s = nc / 4;
     if (max_s < 1) max_s = 1;
     if (s > max_s) s = max_s;
+  } else {
+    const int64_t need = (tiles + G - 1) / G;
+    const int64_t rounds = (need + num_sms - 1) / num_sms;
+    groups = rounds * num_sms < tiles ? rounds * num_sms : tiles;
   }
   int64_t c = (nc + s - 1) / s;
   s = (nc + c - 1) / c;
-  *splits = (int)s;
-  *cps = (int)c;
-  *n_chunks = (int)nc;
-  *n_tiles = (int)tiles;
+  p->splits = (int)s;
+  p->chunks_per_split = (int)c;
+  p->n_chunks = (int)nc;
+  p->n_tiles = (int)tiles;
+  p->n_groups = (int)groups;
 }
 
 int product_split_count(int64_t M, int64_t N, int Dp, bool x3, int num_sms) {
   ProdCfgRt c = product_cfg(Dp, x3);
   if (!c.ok) return 0;
-  int s, cps, nc, nt;
-  plan_splits(M, N, c.bn, num_sms, &s, &cps, &nc, &nt);
-  return s;
+  ProductParams p;
+  plan_work(M, N, c.bn, c.g, num_sms, &p);
+  return p.splits;
 }
 
-template <int DP, int BN, int STAGES, bool X3, bool REDUCE, int NXB>
+template <int DP, int BN, int STAGES, bool X3, bool REDUCE, int G>
 static int run_kernel(const CUtensorMap& mx, const CUtensorMap& mfh, const CUtensorMap& mfl,
                       const CUtensorMap& mch, const CUtensorMap& mcl, const ProductParams& p,
                       int grid, cudaStream_t stream) {
-  using Cfg = ProductCfg<DP, BN, STAGES, X3, REDUCE, NXB>;
-  auto kern = relu_product_kernel<DP, BN, STAGES, X3, REDUCE, NXB>;
+  using Cfg = ProductCfg<DP, BN, STAGES, X3, REDUCE, G>;
+  auto kern = relu_product_kernel<DP, BN, STAGES, X3, REDUCE, G>;
   // once per device (and before any stream capture: the first call of a shape runs eagerly)
   static bool attr_set[64] = {};
   int dev = 0;
@@ -137,36 +145,36 @@ static int run_kernel(const CUtensorMap& mx, const CUtensorMap& mfh, const CUten
   return (int)cudaGetLastError();
 }
 
-#define SB_PRODUCT_CASE(DPV, BNV, STV, X3V, REDV, NXBV)                                        \
-  if (Dp == DPV && bn == BNV && stages == STV && x3 == X3V && nxb == NXBV)                     \
-    return run_kernel<DPV, BNV, STV, X3V, REDV, NXBV>(mx, mfh, mfl, mch, mcl, p, grid, stream);
+#define SB_PRODUCT_CASE(DPV, BNV, STV, X3V, REDV, GV)                                          \
+  if (Dp == DPV && c.bn == BNV && c.stages == STV && x3 == X3V && c.g == GV)                   \
+    return run_kernel<DPV, BNV, STV, X3V, REDV, GV>(mx, mfh, mfl, mch, mcl, p, grid, stream);
 
-static int dispatch_product(int Dp, int bn, int stages, int nxb, bool x3, const CUtensorMap& mx,
+static int dispatch_product(int Dp, const ProdCfgRt& c, bool x3, const CUtensorMap& mx,
                             const CUtensorMap& mfh, const CUtensorMap& mfl, const CUtensorMap& mch,
                             const CUtensorMap& mcl, const ProductParams& p, int grid,
                             cudaStream_t stream) {
-  SB_PRODUCT_CASE(16, 128, 6, false, false, 2)
-  SB_PRODUCT_CASE(32, 128, 4, false, false, 2)
+  SB_PRODUCT_CASE(16, 128, 4, false, false, 8)
+  SB_PRODUCT_CASE(32, 128, 3, false, false, 4)
   SB_PRODUCT_CASE(64, 128, 2, false, false, 2)
   SB_PRODUCT_CASE(128, 64, 2, false, false, 1)
-  SB_PRODUCT_CASE(16, 64, 6, true, false, 2)
-  SB_PRODUCT_CASE(32, 64, 4, true, false, 2)
+  SB_PRODUCT_CASE(16, 64, 4, true, false, 8)
+  SB_PRODUCT_CASE(32, 64, 2, true, false, 4)
   SB_PRODUCT_CASE(64, 64, 2, true, false, 1)
   return -1;
 }
 
-static int dispatch_reduce(int Dp, int bn, int stages, int nxb, bool x3, const CUtensorMap& mx,
+static int dispatch_reduce(int Dp, const ProdCfgRt& c, bool x3, const CUtensorMap& mx,
                            const CUtensorMap& mfh, const CUtensorMap& mfl, const CUtensorMap& mch,
                            const CUtensorMap& mcl, const ProductParams& p, int grid,
                            cudaStream_t stream) {
-  SB_PRODUCT_CASE(16, 128, 6, false, true, 2)
-  SB_PRODUCT_CASE(32, 128, 4, false, true, 2)
-  SB_PRODUCT_CASE(64, 128, 3, false, true, 2)
+  SB_PRODUCT_CASE(16, 128, 6, false, true, 8)
+  SB_PRODUCT_CASE(32, 128, 4, false, true, 8)
+  SB_PRODUCT_CASE(64, 128, 3, false, true, 4)
   SB_PRODUCT_CASE(128, 64, 2, false, true, 2)
   SB_PRODUCT_CASE(256, 32, 2, false, true, 1)
-  SB_PRODUCT_CASE(16, 128, 4, true, true, 2)
-  SB_PRODUCT_CASE(32, 128, 3, true, true, 2)
-  SB_PRODUCT_CASE(64, 64, 3, true, true, 1)
+  SB_PRODUCT_CASE(16, 128, 4, true, true, 8)
+  SB_PRODUCT_CASE(32, 128, 3, true, true, 4)
+  SB_PRODUCT_CASE(64, 64, 3, true, true, 2)
   SB_PRODUCT_CASE(128, 32, 2, true, true, 1)
   return -1;
 }
@@ -179,8 +187,7 @@ static CUtensorMapSwizzle row_swizzle(int Dp) {
 int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float* Flo,
                         const float* Cthi, const float* Ctlo, int64_t ldct, int64_t N, int Dp,
                         bool x3, float* ws, int* err, int num_sms, unsigned long long timeout_ns,
-                        cudaStream_t stream, const FinalizeArgs* fin, int* fused,
-                        const unsigned int* stats) {
+                        cudaStream_t stream, const unsigned int* stats) {
   ProdCfgRt c = product_cfg(Dp, x3);
   if (!c.ok) return -1;
   if (M <= 0 || N <= 0 || M >= INT32_MAX || N >= INT32_MAX) return -5;
@@ -196,20 +203,16 @@ int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float
   ProductParams p;
   p.M = (int)M;
   p.N = (int)N;
-  plan_splits(M, N, c.bn, num_sms, &p.splits, &p.chunks_per_split, &p.n_chunks, &p.n_tiles);
+  plan_work(M, N, c.bn, c.g, num_sms, &p);
   p.ws = ws;
   p.partials = nullptr;
   p.err = err;
   p.timeout_ns = timeout_ns;
   p.Xg = X;
   p.stats = stats;
-  p.fuse = (fin != nullptr && p.splits == 1 && Dp <= 32) ? 1 : 0;
-  if (p.fuse) p.fin = *fin;
-  else memset(&p.fin, 0, sizeof(p.fin));
-  if (fused) *fused = p.fuse;
-  const int64_t items = (int64_t)p.n_tiles * p.splits;
+  const int64_t items = (int64_t)p.n_groups * p.splits;
   const int grid = (int)(items < num_sms ? items : num_sms);
-  return dispatch_product(Dp, c.bn, c.stages, c.nxb, x3, mx, mfh, mfl, mch, mcl, p, grid, stream);
+  return dispatch_product(Dp, c, x3, mx, mfh, mfl, mch, mcl, p, grid, stream);
 }
 
 int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float* Flo, int64_t N,
@@ -227,19 +230,17 @@ int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float*
   ProductParams p;
   p.M = (int)M;
   p.N = (int)N;
-  plan_splits(M, N, c.bn, num_sms, &p.splits, &p.chunks_per_split, &p.n_chunks, &p.n_tiles);
+  plan_work(M, N, c.bn, c.g, num_sms, &p);
   p.ws = nullptr;
   p.Xg = X;
   p.stats = nullptr;
-  p.fuse = 0;
-  memset(&p.fin, 0, sizeof(p.fin));
   p.partials = partials;
   p.err = err;
   p.timeout_ns = timeout_ns;
-  const int64_t items = (int64_t)p.n_tiles * p.splits;
+  const int64_t items = (int64_t)p.n_groups * p.splits;
   const int grid = (int)(items < num_sms ? items : num_sms);
   *grid_out = grid;
-  return dispatch_reduce(Dp, c.bn, c.stages, c.nxb, x3, mx, mfh, mfl, mfh, mfh, p, grid, stream);
+  return dispatch_reduce(Dp, c, x3, mx, mfh, mfl, mfh, mfh, p, grid, stream);
 }
 
 }  // namespace sb
