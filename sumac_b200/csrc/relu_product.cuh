@@ -26,15 +26,16 @@
 //                group tcgen05.ld of each Y_g -> global
 //   warp 10      3xTF32: splits each X tile into tf32 hi / lo halves in shared memory;
 //                TF32 product: converts each C chunk to fp16 for the second MMA
-//   warp 11      second-MMA issuer (one thread, product mode): Y_g += R C_c with R read from
-//                TMEM once the epilogue has rewritten that S as R = ReLU(S); its commit hands
-//                the S buffer back to warp 1.
+//   warps 11-12  second-MMA issuers (one thread each, product mode, even / odd tiles of the
+//                group): Y_g += R C_c with R read from TMEM once the epilogue has rewritten
+//                that S as R = ReLU(S); the commit hands the S buffer back to warp 1.
 //
 // Cost model (measured on B200): at small rank the kernel is bound by the serial latency of
-// issuing MMAs (the second MMA has N = Dp, so it needs BN / 16 fp16 or BN / 8 tf32 instructions
-// per pair) and by the epilogue's TMEM round trip, not by tensor throughput; two issuing threads
-// and the resident tile groups (a chunk copy from L2 takes 1.5-3 us to land when every SM reads
-// the same lines) keep those two off each other's critical path.
+// issuing tcgen05 instructions (~50 ns per MMA or commit from one thread, whatever N <= 64;
+// the second MMA has N = Dp and needs BN / 16 fp16 or BN / 8 tf32 instructions per pair) and by
+// the epilogue's TMEM round trip, not by tensor throughput. Three issuing threads and the
+// resident tile groups (a chunk copy from L2 takes 1.5-3 us to land when every SM reads the
+// same lines) keep those off each other's critical path.
 //
 // Precision: X3=false is TF32 for S = X F^T (the tensor core reads the fp32 bits as tf32), and
 // the second MMA runs in fp16 (same 10-bit mantissa) with R and C scaled by exact powers of two
@@ -109,8 +110,10 @@ struct ProductCfg {
   static constexpr int EPI_WARPS = 8;                     // two per TMEM lane quadrant
   static constexpr int EPI_THREADS = 32 * EPI_WARPS;
   static constexpr bool AUX = X3 || H16;                  // warp 10: X splitter / C converter
-  static constexpr int MMA2_WARP = 11;                    // product mode: second-MMA issuer
-  static constexpr int THREADS = REDUCE ? 64 + EPI_THREADS + (AUX ? 32 : 0) : 32 * 12;
+  // product mode: second-MMA issuers, warp MMA2_WARP + i takes the tiles gi with gi % N2 == i
+  static constexpr int MMA2_WARP = 11;
+  static constexpr int N2 = 2;
+  static constexpr int THREADS = REDUCE ? 64 + EPI_THREADS + (AUX ? 32 : 0) : 32 * (11 + N2);
   static constexpr int EPI_COLS = BN / 2;                 // S columns per epilogue warp
   static_assert(EPI_COLS % 16 == 0, "epilogue column split");
   static constexpr int LDW = EPI_COLS % 32 == 0 ? 32 : 16;  // tcgen05.ld/st width used
@@ -164,8 +167,8 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
   uint64_t* x_empty = x_ready + G;          // [G] last MMA reading the X slot completed
   uint64_t* y_full = x_empty + G;           // [G] Y accumulator complete
   uint64_t* y_empty = y_full + G;           // [G] Y accumulator read out
-  uint64_t* drain = y_empty + G;            // [2] each MMA thread's own MMAs completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
+  uint64_t* drain = y_empty + G;            // [1 + N2] each MMA thread's own MMAs completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1 + Cfg::N2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   double* red = reinterpret_cast<double*>(smem + Cfg::SMEM_DATA + 768);  // [EPI_WARPS][2]
 
@@ -176,7 +179,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], REDUCE ? 1 : Cfg::N2);
       mbar_init(&c16_ready[s], 32);
     }
     for (int b = 0; b < NBUF; ++b) {
@@ -191,8 +194,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
       mbar_init(&y_full[g], 1);
       mbar_init(&y_empty[g], Cfg::EPI_THREADS);
     }
-    mbar_init(&drain[0], 1);
-    mbar_init(&drain[1], 1);
+    for (int i = 0; i <= Cfg::N2; ++i) mbar_init(&drain[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -333,8 +335,10 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
       mma_commit(&drain[0]);
       mbar_drain(&drain[0], 0);
     }
-  } else if (!REDUCE && warp == Cfg::MMA2_WARP) {
+  } else if (!REDUCE && warp >= Cfg::MMA2_WARP && warp < Cfg::MMA2_WARP + Cfg::N2) {
     // ------------------------------------------------------------------ second MMA (Y += R C)
+    // issuer `me` owns the Y slots gi with gi % N2 == me
+    const int me = warp - Cfg::MMA2_WARP;
     if (lane == 0) {
       const uint32_t sSt_addr = smem_u32(sStage);
       uint32_t pair = 0, chunk = 0;
@@ -346,9 +350,12 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
         for (int c = w.c0; c < w.c1 && ok; ++c, ++chunk) {
           const int stage = chunk % STAGES;
           const uint32_t stg = sSt_addr + stage * Cfg::STAGE_ALLOC;
-          if (Cfg::H16 && !mbar_wait(&c16_ready[stage], (chunk / STAGES) & 1, abort_flag, p.err,
-                                     DEV_TIMEOUT_FULL, p.timeout_ns)) { ok = false; break; }
+          // every issuer waits for the chunk, even one that owns no tile of this group: its
+          // commit on `empty` below must not run ahead into a later phase of the barrier
+          if (!mbar_wait(Cfg::H16 ? &c16_ready[stage] : &full[stage], (chunk / STAGES) & 1,
+                         abort_flag, p.err, DEV_TIMEOUT_FULL, p.timeout_ns)) { ok = false; break; }
           for (int gi = 0; gi < w.ntiles; ++gi, ++pair) {
+            if (gi % Cfg::N2 != me) continue;
             const uint32_t buf = pair % NBUF;
             const bool first = c == w.c0;
             if (!mbar_wait(&r_ready[buf], (pair / NBUF) & 1, abort_flag, p.err, DEV_TIMEOUT_RREADY,
@@ -390,18 +397,18 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
               }
             }
             mma_commit(&s_free[buf]);
-            // every first MMA of this chunk completed before the epilogue released its S, so
-            // this commit covers the last reader of the stage
-            if (gi == w.ntiles - 1) mma_commit(&empty[stage]);
             if (c == w.c1 - 1) mma_commit(&y_full[gi]);
           }
+          // every first MMA of this chunk completed before the epilogue released its S, so the
+          // N2 issuers' commits together cover the last readers of the stage
+          if (ok) mma_commit(&empty[stage]);
         }
         const uint32_t mask = (1u << w.ntiles) - 1u;
         slot_par ^= mask;
         slot_used |= mask;
       }
-      mma_commit(&drain[1]);
-      mbar_drain(&drain[1], 0);
+      mma_commit(&drain[1 + me]);
+      mbar_drain(&drain[1 + me], 0);
     }
   } else if (warp >= 2 && warp < 2 + Cfg::EPI_WARPS) {
     // ------------------------------------------------------------------ epilogue (warps 2..9)
