@@ -116,7 +116,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
@@ -231,7 +231,7 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     lib = _native.lib()
-    launches0 = lib.sumac_kernel_launches()
+    launches0 = lib.sumac_kernel_launches() + st.replayed_launches
     ev0, ev1 = torch.cuda.Event(True), torch.cuda.Event(True)
     with ClockSampler(local) as clk:
         ev0.record()
@@ -239,7 +239,8 @@ def run_ours(args):
             st.iteration(it, draw_perm(m, gen_rows, dev), draw_perm(n, gen_cols, dev))
         ev1.record()
         torch.cuda.synchronize()
-    launches = lib.sumac_kernel_launches() - launches0
+    # graph replays launch the kernels captured once: the library counts launches at capture
+    launches = lib.sumac_kernel_launches() + st.replayed_launches - launches0
     ms = ev0.elapsed_time(ev1)
     if world > 1:
         t = torch.tensor([ms], device=dev)
@@ -460,7 +461,7 @@ def run_product_only(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="c4")

@@ -495,6 +495,41 @@ void launch_operand_stats(const float* F, int64_t N, int Dp, const float* C, int
 //   GRAD / STORE: corr_j += (L - v - ReLU(L)) C_i; out_j (+)= scale (Y + corr)
 // One group of G = min(32, Dp/4) lanes owns a row, one float4 slice (or two) per lane.
 // ============================================================================================
+// Entries of a row beyond this many are shared by the whole warp in finalize_kernel.
+constexpr int FIN_K0 = 8;
+
+// <x, f> over V float4 slices (this lane's part of a row)
+template <int V>
+__device__ __forceinline__ float dot4v(const float4* x, const float4* f) {
+  float s = 0.f;
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    s = fmaf(x[v].x, f[v].x, s);
+    s = fmaf(x[v].y, f[v].y, s);
+    s = fmaf(x[v].z, f[v].z, s);
+    s = fmaf(x[v].w, f[v].w, s);
+  }
+  return s;
+}
+
+// acc += coef * c over V float4 slices
+template <int V>
+__device__ __forceinline__ void axpy4v(float coef, const float4* c, float4* acc) {
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    acc[v].x = fmaf(coef, c[v].x, acc[v].x);
+    acc[v].y = fmaf(coef, c[v].y, acc[v].y);
+    acc[v].z = fmaf(coef, c[v].z, acc[v].z);
+    acc[v].w = fmaf(coef, c[v].w, acc[v].w);
+  }
+}
+
+// Support correction coefficient of one entry (value val, prediction L): SALSA adds
+// (S - L + ReLU(L)) C_i (training/salsa.py:100-111), the gradient modes (L - S - ReLU(L)) C_i.
+__device__ __forceinline__ float support_coef(int mode, float val, float L) {
+  return (mode == FIN_SALSA) ? (val - L + fmaxf(L, 0.f)) : (L - val - fmaxf(L, 0.f));
+}
+
 template <int DP>
 __global__ void finalize_kernel(FinalizeArgs a) {
   constexpr int G = DP / 4 < 32 ? DP / 4 : 32;  // lanes per row
@@ -529,22 +564,24 @@ __global__ void finalize_kernel(FinalizeArgs a) {
     if (a.rowptr) {
       const int e0 = active ? a.rowptr[j] : 0;
       const int ne = active ? a.rowptr[j + 1] - e0 : 0;
-      int nmax = ne;
+      // light part: each row's own lane group takes its first FIN_K0 entries, four per round
+      // (independent loads, fixed accumulation order)
+      const int nl = (RPW == 1 || ne < FIN_K0) ? ne : FIN_K0;
+      int nmax = nl;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) nmax = max(nmax, __shfl_xor_sync(0xffffffffu, nmax, o));
-      // four entries per round: their loads are independent, the accumulation order is fixed
       for (int q0 = 0; q0 < nmax; q0 += 4) {
         int2 en[4];
         float4 f[4][V], c[4][V];
         float part[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const bool has = q0 + u < ne;
+          const bool has = q0 + u < nl;
           en[u] = has ? a.ent[e0 + q0 + u] : make_int2(0, 0);
         }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const bool has = q0 + u < ne;
+          const bool has = q0 + u < nl;
           const float4* frow = reinterpret_cast<const float4*>(a.F + (int64_t)en[u].x * DP);
           const float4* crow = reinterpret_cast<const float4*>(a.Cm + (int64_t)en[u].x * DP);
 #pragma unroll
@@ -554,35 +591,81 @@ __global__ void finalize_kernel(FinalizeArgs a) {
           }
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          float s = 0.f;
-#pragma unroll
-          for (int v = 0; v < V; ++v) {
-            s = fmaf(x[v].x, f[u][v].x, s);
-            s = fmaf(x[v].y, f[u][v].y, s);
-            s = fmaf(x[v].z, f[u][v].z, s);
-            s = fmaf(x[v].w, f[u][v].w, s);
-          }
-          part[u] = s;
-        }
+        for (int u = 0; u < 4; ++u) part[u] = dot4v<V>(x, f[u]);
 #pragma unroll
         for (int o = G / 2; o > 0; o >>= 1) {
 #pragma unroll
           for (int u = 0; u < 4; ++u) part[u] += __shfl_xor_sync(0xffffffffu, part[u], o);
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          if (q0 + u < ne) {
-            const float L = part[u];
-            const float val = __int_as_float(en[u].y);
-            const float coef = (a.mode == FIN_SALSA) ? (val - L + fmaxf(L, 0.f))
-                                                     : (L - val - fmaxf(L, 0.f));
+        for (int u = 0; u < 4; ++u)
+          if (q0 + u < nl) axpy4v<V>(support_coef(a.mode, __int_as_float(en[u].y), part[u]), c[u], cor);
+      }
+      // heavy part (power-law rows): the whole warp shares the rest of one row at a time, one
+      // entry per lane group and round, then the groups' partial corrections are summed
+      if (RPW > 1) {
+        unsigned heavy = __ballot_sync(0xffffffffu, gl == 0 && ne > FIN_K0);
+        while (heavy) {
+          const int src = __ffs(heavy) - 1;
+          heavy &= heavy - 1;
+          const int hg = src / G;
+          const int hb = __shfl_sync(0xffffffffu, e0, src) + FIN_K0;
+          const int hn = __shfl_sync(0xffffffffu, ne, src) - FIN_K0;
+          float4 hx[V], hcor[V];
+#pragma unroll
+          for (int v = 0; v < V; ++v) {
+            const int sl = hg * G + gl;
+            hx[v] = make_float4(__shfl_sync(0xffffffffu, x[v].x, sl), __shfl_sync(0xffffffffu, x[v].y, sl),
+                                __shfl_sync(0xffffffffu, x[v].z, sl), __shfl_sync(0xffffffffu, x[v].w, sl));
+            hcor[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+          for (int q0 = 0; q0 < hn; q0 += 2 * RPW) {
+            int2 en[2];
+            float4 f[2][V], c[2][V];
+            float part[2];
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int q = q0 + u * RPW + gw;
+              en[u] = q < hn ? a.ent[hb + q] : make_int2(0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const bool has = q0 + u * RPW + gw < hn;
+              const float4* frow = reinterpret_cast<const float4*>(a.F + (int64_t)en[u].x * DP);
+              const float4* crow = reinterpret_cast<const float4*>(a.Cm + (int64_t)en[u].x * DP);
+#pragma unroll
+              for (int v = 0; v < V; ++v) {
+                f[u][v] = has ? frow[gl + v * G] : make_float4(0.f, 0.f, 0.f, 0.f);
+                c[u][v] = has ? crow[gl + v * G] : make_float4(0.f, 0.f, 0.f, 0.f);
+              }
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u) part[u] = dot4v<V>(hx, f[u]);
+#pragma unroll
+            for (int o = G / 2; o > 0; o >>= 1) {
+#pragma unroll
+              for (int u = 0; u < 2; ++u) part[u] += __shfl_xor_sync(0xffffffffu, part[u], o);
+            }
+#pragma unroll
+            for (int u = 0; u < 2; ++u)
+              if (q0 + u * RPW + gw < hn)
+                axpy4v<V>(support_coef(a.mode, __int_as_float(en[u].y), part[u]), c[u], hcor);
+          }
+#pragma unroll
+          for (int o = G; o < 32; o <<= 1) {
 #pragma unroll
             for (int v = 0; v < V; ++v) {
-              cor[v].x = fmaf(coef, c[u][v].x, cor[v].x);
-              cor[v].y = fmaf(coef, c[u][v].y, cor[v].y);
-              cor[v].z = fmaf(coef, c[u][v].z, cor[v].z);
-              cor[v].w = fmaf(coef, c[u][v].w, cor[v].w);
+              hcor[v].x += __shfl_xor_sync(0xffffffffu, hcor[v].x, o);
+              hcor[v].y += __shfl_xor_sync(0xffffffffu, hcor[v].y, o);
+              hcor[v].z += __shfl_xor_sync(0xffffffffu, hcor[v].z, o);
+              hcor[v].w += __shfl_xor_sync(0xffffffffu, hcor[v].w, o);
+            }
+          }
+          if (gw == hg) {
+#pragma unroll
+            for (int v = 0; v < V; ++v) {
+              cor[v].x += hcor[v].x; cor[v].y += hcor[v].y;
+              cor[v].z += hcor[v].z; cor[v].w += hcor[v].w;
             }
           }
         }

@@ -87,6 +87,8 @@ class SalsaState:
             if torch.cuda.is_available() else None
         self.use_graph = True
         self.graph = None
+        self.graph_launches = 0      # library kernels captured in the graph
+        self.replayed_launches = 0   # library kernels launched by graph replays
         self.eager_done = False
         self.perm_r = torch.empty(m, dtype=torch.int64, device=dev)
         self.perm_c = torch.empty(n, dtype=torch.int64, device=dev)
@@ -110,10 +112,13 @@ class SalsaState:
             self.perm_r.copy_(perm_r)
             self.perm_c.copy_(perm_c)
             g = torch.cuda.CUDAGraph()
+            n0 = _native.lib().sumac_kernel_launches()
             with torch.cuda.graph(g):
                 self._body(self.perm_r, self.perm_c)
+            self.graph_launches = _native.lib().sumac_kernel_launches() - n0
             self.graph = g
             g.replay()
+            self.replayed_launches += self.graph_launches
             return
         if self.graph is None:
             self._body(perm_r, perm_c)
@@ -122,6 +127,7 @@ class SalsaState:
         self.perm_r.copy_(perm_r)
         self.perm_c.copy_(perm_c)
         self.graph.replay()
+        self.replayed_launches += self.graph_launches
 
     def _body(self, perm_r: Tensor, perm_c: Tensor) -> None:
         nb = self.nb
