@@ -258,8 +258,10 @@ static constexpr int PREP_ROWS = 64;
 int salsa_gram_parts(int64_t b) { return cdiv64(b, PREP_ROWS) < 1 ? 1 : cdiv64(b, PREP_ROWS); }
 
 // Register LU with partial pivoting of the D x D matrix G (padded with an identity block),
-// by one warp: lane i holds row i, the pivot row is broadcast by shuffles. Writes the packed L\U
-// factors and the pivot sequence (first maximal |pivot| wins, as LAPACK getrf).
+// by one warp: lane i keeps row i of G in registers for the whole factorisation; the row
+// exchanges of getrf are tracked as a permutation instead of being moved between lanes. Writes
+// the packed L\U factors in pivoted row order and getrf's pivot sequence (at step k the first
+// row, in the current exchanged order, of maximal |a_k| wins).
 template <int D>
 __device__ __forceinline__ void warp_lu(const double* __restrict__ G, int d, double* LU, int* piv,
                                         int* err) {
@@ -269,27 +271,33 @@ __device__ __forceinline__ void warp_lu(const double* __restrict__ G, int d, dou
 #pragma unroll
   for (int j = 0; j < D; ++j)
     a[j] = (lane < d && j < d) ? G[lane * d + j] : (lane == j ? 1.0 : 0.0);
+  int pos = lane;       // this lane's row position in the exchanged order
+  bool done = lane >= D;  // row already used as a pivot (or not a row)
 #pragma unroll
   for (int k = 0; k < D; ++k) {
-    double best = (lane >= k && lane < D) ? fabs(a[k]) : -1.0;
-    int bi = lane;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const double ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
-    }
+    // the largest |a_k| among the remaining rows: compare the bit patterns of the non-negative
+    // doubles (monotonic), high word first; ties go to the smallest exchanged position
+    const unsigned long long key =
+        done ? 0ull : (unsigned long long)__double_as_longlong(fabs(a[k]));
+    const unsigned hi = (unsigned)(key >> 32), lo = (unsigned)key;
+    const unsigned mhi = __reduce_max_sync(0xffffffffu, done ? 0u : hi);
+    const bool c1 = !done && hi == mhi;
+    const unsigned mlo = __reduce_max_sync(0xffffffffu, c1 ? lo : 0u);
+    const bool c2 = c1 && lo == mlo;
+    const unsigned mpos = __reduce_min_sync(0xffffffffu, c2 ? (unsigned)pos : 0xffffffffu);
+    const bool me = c2 && (unsigned)pos == mpos;
+    const int src = __ffs(__ballot_sync(0xffffffffu, me)) - 1;  // lane holding the pivot row
+    // getrf exchanges positions k and mpos: the row at position k moves to mpos
     if (lane == 0) {
-      piv[k] = bi;
-      if (best == 0.0 && err) atomicCAS(err, 0, DEV_SINGULAR);
+      piv[k] = (int)mpos;
+      if (mhi == 0u && mlo == 0u && err) atomicCAS(err, 0, DEV_SINGULAR);
     }
-    const int src = lane == k ? bi : (lane == bi ? k : lane);
-#pragma unroll
-    for (int j = 0; j < D; ++j) a[j] = __shfl_sync(0xffffffffu, a[j], src);
+    if (!done && pos == k) pos = (int)mpos;
+    if (me) { pos = k; done = true; }
     double u[D];
 #pragma unroll
-    for (int j = k; j < D; ++j) u[j] = __shfl_sync(0xffffffffu, a[j], k);
-    if (lane > k && lane < D) {
+    for (int j = k; j < D; ++j) u[j] = __shfl_sync(0xffffffffu, a[j], src);
+    if (!done) {
       const double l = a[k] / u[k];
       a[k] = l;
 #pragma unroll
@@ -298,7 +306,7 @@ __device__ __forceinline__ void warp_lu(const double* __restrict__ G, int d, dou
   }
   if (lane < D) {
 #pragma unroll
-    for (int j = 0; j < D; ++j) LU[lane * D + j] = a[j];
+    for (int j = 0; j < D; ++j) LU[pos * D + j] = a[j];
   }
 }
 
@@ -349,7 +357,7 @@ __global__ void salsa_gram_kernel(const float* __restrict__ Ffix, const int64_t*
   __threadfence();
   for (int e = threadIdx.x; e < dd; e += blockDim.x) {
     double s = 0.0;
-#pragma unroll 4
+#pragma unroll 8
     for (int q = 0; q < (int)gridDim.x; ++q) s += __ldcg(&parts[(size_t)q * dd + e]);
     sG[e] = s;
   }
