@@ -1,0 +1,218 @@
+"""Row-sharded SALSA over several GPUs (one process per GPU, torch.distributed with NCCL).
+
+The reference's SALSA (src/sumac/training/salsa.py:212-355) updates, for every block k of an
+iteration, all rows of B against the block's rows A_I of A, then all rows of A against the block's
+rows B_J of B. Every row's update depends only on its own row, on the block rows of the fixed factor
+and on that row's entries of S (salsa.py:84-166). So the work shards by rows with no partial sums:
+
+* rank r owns the contiguous rows [lo, hi) of A and of B (and their momenta), and keeps, for each
+  update direction, the entries of S whose updated row it owns (their fixed-row index stays global);
+* before a block update, the block rows of the fixed factor (b x Dp, ~90 KB at C4's shapes) are
+  assembled on every rank: each rank writes the rows it owns into a zero buffer and an allreduce
+  (sum) completes it. With one nonzero contributor per element the sum is exact, so every rank
+  holds bit-identical block rows, Gram matrix and least-squares map;
+* each rank then runs the single-GPU block update (Gram + solve, fused product, finalize) on its
+  own rows only.
+
+Permutations come from the same seeded generators on every rank, so all ranks agree on the blocks
+without communication. The factors are all-gathered only where the caller needs them whole
+(evaluation, the end of the run).
+"""
+from __future__ import annotations
+
+import time
+
+import numpy as np
+import torch
+import torch.distributed as dist
+from torch import Tensor
+
+from . import _native, ops
+from .config import SumacConfig
+from .data import SparseDirection
+from .metrics import Evaluator
+from .salsa import draw_perm, init_salsa_factors, unbias_values
+
+
+def shard_range(total: int, rank: int, world: int) -> tuple[int, int]:
+    """Rows [lo, hi) of a `total`-row factor owned by `rank` (balanced contiguous ranges)."""
+    return total * rank // world, total * (rank + 1) // world
+
+
+def split_direction(fixed: Tensor, out: Tensor, lo: int, hi: int) -> Tensor:
+    """Mask of the entries whose updated row `out` lies in this rank's range [lo, hi)."""
+    return (out >= lo) & (out < hi)
+
+
+def assemble_rows(local: Tensor, lo: int, hi: int, rows: Tensor, out: Tensor, group=None) -> None:
+    """out[p] = F[rows[p]] for a factor F row-sharded over the group, this rank holding
+    F[lo:hi] as `local`: the rows this rank owns are written, the others are zero, and an
+    allreduce(sum) completes the buffer on every rank (exact: one nonzero term per element).
+    No host synchronisation, so it can be captured in a CUDA graph."""
+    idx = (rows - lo).clamp(0, max(hi - lo - 1, 0))
+    own = ((rows >= lo) & (rows < hi)).unsqueeze(1)
+    torch.where(own, local[idx], torch.zeros((), dtype=local.dtype, device=local.device), out=out)
+    dist.all_reduce(out, group=group)
+
+
+def gather_rows(local: Tensor, total: int, group=None) -> Tensor:
+    """All-gather a row-sharded factor (contiguous balanced shards) into the whole factor."""
+    world = dist.get_world_size(group)
+    rmax = max(shard_range(total, r, world)[1] - shard_range(total, r, world)[0]
+               for r in range(world))
+    buf = torch.zeros((rmax,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    buf[:local.shape[0]] = local
+    parts = [torch.empty_like(buf) for _ in range(world)]
+    dist.all_gather(parts, buf, group=group)
+    return torch.cat([parts[r][:shard_range(total, r, world)[1] - shard_range(total, r, world)[0]]
+                      for r in range(world)])
+
+
+class ShardedSalsaState:
+    """Device state of one rank of a row-sharded SALSA run."""
+
+    def __init__(self, S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfig,
+                 A: Tensor, B: Tensor, group=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.d = cfg.rank
+        self.Dp = ops.padded_rank(self.d)
+        self.m, self.n = m, n
+        self.nb = cfg.num_blocks
+        self.prec = cfg.precision()
+        self.ra = shard_range(m, self.rank, self.world)
+        self.rb = shard_range(n, self.rank, self.world)
+        if self.ra[1] <= self.ra[0] or self.rb[1] <= self.rb[0]:
+            raise ValueError(f"more ranks ({self.world}) than rows of a factor ({m} x {n})")
+        dev = S_value.device
+        self.Ap = ops.pad_factor(A[self.ra[0]:self.ra[1]].to(torch.float32), self.Dp)
+        self.Bp = ops.pad_factor(B[self.rb[0]:self.rb[1]].to(torch.float32), self.Dp)
+        self.dA = torch.zeros_like(self.Ap)
+        self.dB = torch.zeros_like(self.Bp)
+        i, j = S_index[0], S_index[1]
+        # B-update: fixed = rows of A (global index), updated = this rank's rows of B
+        kb = split_direction(i, j, *self.rb)
+        self.dir_b = SparseDirection(i[kb], j[kb] - self.rb[0], S_value[kb], m,
+                                     self.rb[1] - self.rb[0], self.nb)
+        # A-update: fixed = rows of B (global index), updated = this rank's rows of A
+        ka = split_direction(j, i, *self.ra)
+        self.dir_a = SparseDirection(j[ka], i[ka] - self.ra[0], S_value[ka], n,
+                                     self.ra[1] - self.ra[0], self.nb)
+        self.FI_b = torch.zeros((self.dir_b.block_size, self.Dp), dtype=torch.float32, device=dev)
+        self.FI_a = torch.zeros((self.dir_a.block_size, self.Dp), dtype=torch.float32, device=dev)
+        self.ident = torch.arange(max(self.dir_a.block_size, self.dir_b.block_size),
+                                  dtype=torch.int64, device=dev)
+        self.momentum = float(cfg.momentum)
+        self.lrate = float(np.float32(cfg.learning_rate))
+        self.unbias = torch.empty(self.nb, dtype=torch.float32, device=dev)
+        self.unbias_host = torch.empty(self.nb, dtype=torch.float32).pin_memory()
+        self.perm_r = torch.empty(m, dtype=torch.int64, device=dev)
+        self.perm_c = torch.empty(n, dtype=torch.int64, device=dev)
+        L = _native.lib()
+        self.ws_b = ops._ws(dev, L.sumac_salsa_update_workspace_bytes(
+            self.rb[1] - self.rb[0], self.dir_b.block_size, self.d, self.prec), "salsa_b")
+        self.ws_a = ops._ws(dev, L.sumac_salsa_update_workspace_bytes(
+            self.ra[1] - self.ra[0], self.dir_a.block_size, self.d, self.prec), "salsa_a")
+        self.use_graph = True
+        self.graph = None
+        self.eager_done = False
+        self.graph_launches = 0
+        self.replayed_launches = 0
+
+    def iteration(self, it: int, perm_r: Tensor, perm_c: Tensor) -> None:
+        """One SALSA iteration on this rank's rows: eager the first time, then replays of a CUDA
+        graph of the whole iteration (CSR rebuilds, assemblies with their allreduces, updates)."""
+        nb = self.nb
+        self.unbias_host.copy_(torch.from_numpy(unbias_values(self.momentum, 1 + (it - 1) * nb, nb)))
+        self.unbias.copy_(self.unbias_host, non_blocking=True)
+        if not self.use_graph or self.graph is None:
+            if self.use_graph and self.eager_done:
+                self.perm_r.copy_(perm_r)
+                self.perm_c.copy_(perm_c)
+                g = torch.cuda.CUDAGraph()
+                n0 = _native.lib().sumac_kernel_launches()
+                with torch.cuda.graph(g):
+                    self._body(self.perm_r, self.perm_c)
+                self.graph_launches = _native.lib().sumac_kernel_launches() - n0
+                self.graph = g
+                g.replay()
+                self.replayed_launches += self.graph_launches
+                return
+            self._body(perm_r, perm_c)
+            self.eager_done = True
+            return
+        self.perm_r.copy_(perm_r)
+        self.perm_c.copy_(perm_c)
+        self.graph.replay()
+        self.replayed_launches += self.graph_launches
+
+    def _body(self, perm_r: Tensor, perm_c: Tensor) -> None:
+        self.dir_b.rebuild(perm_r)
+        self.dir_a.rebuild(perm_c)
+        for k in range(self.nb):
+            rows = self.dir_b.block_rows(perm_r, k)
+            b = rows.numel()
+            if b > 0:
+                assemble_rows(self.Ap, self.ra[0], self.ra[1], rows, self.FI_b[:b], self.group)
+                ops.salsa_block_update(self.FI_b, self.ident[:b], self.Bp, self.dB, self.d,
+                                       self.dir_b.block_rowptr(k), self.dir_b.ent, self.momentum,
+                                       self.lrate, self.unbias[k:k + 1], self.prec, self.ws_b)
+            rows = self.dir_a.block_rows(perm_c, k)
+            b = rows.numel()
+            if b > 0:
+                assemble_rows(self.Bp, self.rb[0], self.rb[1], rows, self.FI_a[:b], self.group)
+                ops.salsa_block_update(self.FI_a, self.ident[:b], self.Ap, self.dA, self.d,
+                                       self.dir_a.block_rowptr(k), self.dir_a.ent, self.momentum,
+                                       self.lrate, self.unbias[k:k + 1], self.prec, self.ws_a)
+
+    def factors(self) -> tuple[Tensor, Tensor]:
+        """The whole factors (all-gathered), on every rank."""
+        A = gather_rows(self.Ap, self.m, self.group)[:, :self.d].contiguous()
+        B = gather_rows(self.Bp, self.n, self.group)[:, :self.d].contiguous()
+        return A, B
+
+
+def sharded_salsa_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfig,
+                       A_init: Tensor | None = None, B_init: Tensor | None = None, group=None):
+    """salsa_loop with the rows sharded over the process group: same schedule, generators and
+    history as the single-GPU loop; every rank returns the whole factors."""
+    assert cfg.num_blocks is not None and cfg.device is not None
+    gen, gen_rows, gen_cols = cfg.get_generator()
+    dev = cfg.device
+    S_index = S_index.to(dev)
+    S_value = S_value.to(dev)
+    if A_init is None or B_init is None:
+        A, B = init_salsa_factors(S_index, S_value, m, n, cfg.rank, gen)
+    else:
+        A, B = A_init.to(dev), B_init.to(dev)
+    st = ShardedSalsaState(S_index, S_value, m, n, cfg, A, B, group)
+    evaluator = Evaluator(S_index, S_value, cfg.rank, st.prec)
+    draw_perm(m, gen_rows, dev)
+    draw_perm(n, gen_cols, dev)
+    rmse, jacc, errZ = evaluator(ops.pad_factor(A, st.Dp), ops.pad_factor(B, st.Dp))
+    verbose = cfg.verbose and st.rank == 0
+    if verbose:
+        print(f"[epoch 0/{cfg.max_iterations}]: cost = {errZ:.6f}, rmse = {rmse:.6f}, "
+              f"jacc = {jacc:.6f}, time = 0.0000s")
+    hist = {"cost": [], "rmse": [], "jacc": [], "time": []}
+    t0 = time.time()
+    for it in range(1, cfg.max_iterations + 1):
+        perm_r = draw_perm(m, gen_rows, dev)
+        perm_c = draw_perm(n, gen_cols, dev)
+        st.iteration(it, perm_r, perm_c)
+        if cfg.eval_interval is not None and it % cfg.eval_interval == 0:
+            A, B = st.factors()
+            rmse, jacc, errZ = evaluator(ops.pad_factor(A, st.Dp), ops.pad_factor(B, st.Dp))
+            _native.raise_device_error(dev)
+            elapsed = time.time() - t0
+            hist["cost"].append(errZ)
+            hist["rmse"].append(rmse)
+            hist["jacc"].append(jacc)
+            hist["time"].append(elapsed)
+            if verbose:
+                print(f"[epoch {it}/{cfg.max_iterations}]: cost = {errZ:.6f}, rmse = {rmse:.6f}, "
+                      f"jacc = {jacc:.6f}, time = {elapsed:.4f}s")
+    _native.raise_device_error(dev)
+    A, B = st.factors()
+    return A, B, hist

@@ -51,6 +51,11 @@ def _cuda_device(requested: torch.device) -> torch.device:
     return torch.device("cuda", torch.cuda.current_device())
 
 
+def _world_size() -> int:
+    import torch.distributed as dist
+    return dist.get_world_size() if dist.is_available() and dist.is_initialized() else 1
+
+
 def sumac_factorize(*, S_index: Tensor, S_value: Tensor, shape: tuple[int, int],
                     A_init: Tensor | None = None, B_init: Tensor | None = None,
                     config: SumacConfig):
@@ -89,7 +94,13 @@ def sumac_factorize(*, S_index: Tensor, S_value: Tensor, shape: tuple[int, int],
         if config.method == SumacMethod.GD:
             A, B, costs = GD_loop(S_index, S_value, m_eff, n_eff, config, A_init, B_init)
         elif config.method == SumacMethod.SALSA:
-            A, B, costs = salsa_loop(S_index, S_value, m_eff, n_eff, config, A_init, B_init)
+            if _world_size() > 1:
+                # one process per GPU: rows of A and B sharded over the default process group
+                from .shard import sharded_salsa_loop
+                A, B, costs = sharded_salsa_loop(S_index, S_value, m_eff, n_eff, config, A_init,
+                                                 B_init)
+            else:
+                A, B, costs = salsa_loop(S_index, S_value, m_eff, n_eff, config, A_init, B_init)
         else:
             raise NotImplementedError("method must be chosen from GD or SALSA")
         A_ori, B_ori = restore_zero_rows_cols(A, B, m, n, config.rank, row_mask, col_mask)

@@ -1,0 +1,71 @@
+"""Row-sharded SALSA on two GPUs (two NCCL ranks, sumac_b200/shard.py) against the reference's
+own SALSA run (tests/golden/e2e_salsa.npz): the same factors and history as the single-GPU path.
+Skipped when fewer than two GPUs are visible."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from tests.conftest import load_golden
+from tests.helpers import rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    try:
+        import torch.distributed as dist
+        from sumac_b200 import SumacConfig, SumacMethod, sumac_factorize
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                device_id=torch.device("cuda", rank))
+        g = load_golden("e2e_salsa")
+        cfg = SumacConfig(method=SumacMethod.SALSA, rank=int(g["rank"]),
+                          max_iterations=int(g["iters"]), num_blocks=int(g["num_blocks"]),
+                          seed=int(g["seed"]), learning_rate=float(g["lr"]), verbose=False,
+                          perm_device="cpu", eval_interval=1, device=f"cuda:{rank}")
+        dev = torch.device("cuda", rank)
+        A, B, hist = sumac_factorize(S_index=torch.from_numpy(g["S_index"]).to(dev),
+                                     S_value=torch.from_numpy(g["S_value"]).to(dev),
+                                     shape=(int(g["m"]), int(g["n"])),
+                                     A_init=torch.from_numpy(g["A0"]).to(dev),
+                                     B_init=torch.from_numpy(g["B0"]).to(dev), config=cfg)
+        dist.destroy_process_group()
+        q.put((rank, A.cpu().numpy(), B.cpu().numpy(), hist, None))
+    except Exception as e:  # reported to the parent instead of hanging it
+        q.put((rank, None, None, None, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_sharded_salsa_matches_reference_run():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    g = load_golden("e2e_salsa")
+    for rank, A, B, hist, err in res:
+        assert err is None, (rank, err)
+        assert rel_err(A, g["A"]) < 1e-4
+        assert rel_err(B, g["B"]) < 1e-4
+        for key in ("cost", "rmse", "jacc"):
+            np.testing.assert_allclose(hist[key], g[key], rtol=1e-4)
+    # every rank returns the same whole factors
+    assert np.array_equal(res[0][1], res[1][1]) and np.array_equal(res[0][2], res[1][2])
