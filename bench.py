@@ -223,7 +223,12 @@ def run_ours(args):
                       allow_tf32=allow_tf32, device=dev)
     gen, gen_rows, gen_cols = cfg.get_generator()
     A, B = init_salsa_factors(S_index, S_value, m, n, d, gen)
-    st = SalsaState(S_index, S_value, m, n, cfg, A, B)
+    if world > 1:
+        # rows of A and B sharded over the ranks (NCCL), total work fixed: strong scaling
+        from sumac_b200.shard import ShardedSalsaState
+        st = ShardedSalsaState(S_index, S_value, m, n, cfg, A, B)
+    else:
+        st = SalsaState(S_index, S_value, m, n, cfg, A, B)
     for it in range(1, args.warmup + 1):
         st.iteration(it, draw_perm(m, gen_rows, dev), draw_perm(n, gen_cols, dev))
     torch.cuda.synchronize()
@@ -249,13 +254,14 @@ def run_ours(args):
         dist.barrier()
     _native.raise_device_error(dev)
     ms_per_step = ms / args.steps
-    value = world * args.steps / (ms * 1e-3)
+    value = args.steps / (ms * 1e-3)  # whole-job iterations/s (every rank runs every iteration)
 
-    # ---- the fused product alone (one B-update of this workload), CUDA events
+    # ---- the fused product alone (one B-update of this rank's rows), CUDA events
     prec = cfg.precision()
     Dp = ops.padded_rank(d)
     b = (m + nb - 1) // nb
-    rows = draw_perm(m, gen_rows, dev)[:b]
+    n_loc = st.Bp.shape[0]  # this rank's rows of B (all of them on one GPU)
+    rows = torch.randperm(st.Ap.shape[0], device=dev)[:b]
     FI = st.Ap[rows].contiguous()
     x3 = prec == ops.SUMAC_3XTF32
     ldct = (b + 3) // 4 * 4
@@ -268,14 +274,14 @@ def run_ours(args):
         Ctlo = Ct - Cthi
     else:
         Fhi, Flo, Cthi, Ctlo = FI, None, Ct, None
-    splits = lib.sumac_relu_product_splits(n, b, Dp, prec)
-    part = torch.empty(splits * n * Dp + 16, device=dev)
+    splits = lib.sumac_relu_product_splits(n_loc, b, Dp, prec)
+    part = torch.empty(splits * n_loc * Dp + 16, device=dev)
     err = _native.err_word(dev)
     stream = _native.stream_ptr(dev)
     P = _native.ptr
 
     def launch():
-        _native.check(lib.sumac_relu_product(P(st.Bp), n, P(Fhi), P(Flo), P(Cthi), P(Ctlo), ldct,
+        _native.check(lib.sumac_relu_product(P(st.Bp), n_loc, P(Fhi), P(Flo), P(Cthi), P(Ctlo), ldct,
                                              b, Dp, prec, P(part), P(err), stream), "relu_product")
     for _ in range(5):
         launch()
@@ -288,7 +294,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     _native.raise_device_error(dev)
     kernel_ms = k0.elapsed_time(k1) / reps
-    flops = 4.0 * n * b * d
+    flops = 4.0 * n_loc * b * d
     achieved = flops / (kernel_ms * 1e-3) / 1e12
     pk = peaks()
     tf32_peak = pk["bf16_tflops"] / 2.0
@@ -296,10 +302,11 @@ def run_ours(args):
 
     # ---- e2e through the public API with host inputs
     e2e = None
-    if rank == 0 and not args.no_e2e:
+    if not args.no_e2e:
+        # every rank calls the public API (sharded over the process group when world > 1)
         cfg2 = SumacConfig(method=SumacMethod.SALSA, rank=d, num_blocks=nb, seed=0, verbose=False,
                            allow_tf32=allow_tf32, max_iterations=args.steps,
-                           eval_interval=args.steps + 1)
+                           eval_interval=args.steps + 1, device=dev)
         idx_pin = idx_h.pin_memory()
         val_pin = val_h.pin_memory()
         torch.cuda.synchronize()
@@ -307,6 +314,10 @@ def run_ours(args):
         A2, B2, _ = sumac_factorize(S_index=idx_pin, S_value=val_pin, shape=shape, config=cfg2)
         torch.cuda.synchronize()
         t_e2e = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([t_e2e], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            t_e2e = float(t.item())
         h2d = idx_h.numel() * idx_h.element_size() + val_h.numel() * 4
         d2h = (A2.numel() + B2.numel()) * 4
         e2e = {"value": args.steps / t_e2e, "unit": "iter/s",
@@ -315,8 +326,7 @@ def run_ours(args):
                "inputs: copies, validation, pruning, init and CSR setup inside the timed region"}
 
     if rank != 0:
-        if world > 1:
-            dist.destroy_process_group()
+        _teardown(st, world)
         return
     cpu = cpu_baseline(args, idx_np, val_np, shape, d, nb) if not args.no_cpu else None
     clocks = clk.summary()
@@ -324,13 +334,15 @@ def run_ours(args):
         "metric": "fused ReLU(AB^T)-reduce TFLOP/s; GD/SALSA iters/s at 1/2/4/8 B200",
         "value": value, "unit": "iter/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak" if world > 1 else "strong", "vs_baseline": None,
+        "scaling": "strong", "vs_baseline": None,
         "dtype": "tf32" if not x3 else "f32 (3xTF32)", "data": "synthetic (seeded stand-in)",
         "config": {"workload": cfgd["desc"], "m_eff": m, "n_eff": n, "nnz": int(val_np.size),
                    "rank": d, "num_blocks": nb, "method": "SALSA",
-                   "parallelism": "single GPU" if world == 1 else f"{world} independent replicas",
+                   "parallelism": "single GPU" if world == 1 else
+                   f"rows of A and B sharded over {world} GPUs (NCCL allreduce of each block's "
+                   "fixed rows)",
                    "l2": "inputs larger than L2 (CSR of both directions ~0.3 GB per step)"},
-        "fused_product": {"tflops": achieved, "ms_per_launch": kernel_ms, "M": n, "N": b, "d": d,
+        "fused_product": {"tflops": achieved, "ms_per_launch": kernel_ms, "M": n_loc, "N": b, "d": d,
                           "splits": splits, "flops_per_launch": flops},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": tf32_peak, "unit": "TFLOP/s",
                      "frac": achieved / tf32_peak, "traffic": None,
@@ -341,8 +353,18 @@ def run_ours(args):
         "clocks": clocks,
         "gpu_launches": int(launches),
     }
-    print(json.dumps(line))
+    print(json.dumps(line), flush=True)
+    _teardown(st, world)
+
+
+def _teardown(st, world):
+    """Free the CUDA graph (it holds captured NCCL collectives) before the communicator goes,
+    then leave together: every rank reaches the barrier, then destroys the process group."""
+    st.graph = None
+    torch.cuda.synchronize()
     if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
         dist.destroy_process_group()
 
 
