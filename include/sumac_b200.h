@@ -184,6 +184,15 @@ int sumac_sgd_step(float* p, float* g, float* buf, int64_t n, float lr, float mo
                    const double* sumsq, float max_norm, sumac_stream_t stream);
 int sumac_fill_zero(float* p, int64_t n, sumac_stream_t stream);
 
+/*
+ * Row-sharded factors (multi-GPU SALSA): out[p] = local[rows[p] - lo] (Dp floats) when this rank
+ * owns global row rows[p] (lo <= rows[p] < hi), zero otherwise. An allreduce(sum) of `out` over the
+ * ranks then yields the block rows F[rows] exactly. No counterpart kernel in the reference, whose
+ * multi-GPU SALSA moves whole factors between devices (training/salsa.py:169-209).
+ */
+int sumac_gather_owned_rows(const float* local, int64_t lo, int64_t hi, const int64_t* rows,
+                            int64_t nrows, int Dp, float* out, sumac_stream_t stream);
+
 /* Test hook for the bounded-wait path: waits on *flag (device) for at most timeout_ns and writes
  * a timeout code into *dev_err when nobody sets it. The kernel returns normally either way. */
 int sumac_wait_flag(const int* flag, int* dev_err, unsigned long long timeout_ns,

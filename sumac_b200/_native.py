@@ -34,6 +34,7 @@ _SIGS = {
     "sumac_last_error": (C.c_char_p, []),
     "sumac_set_timeout_ns": (None, [u64]),
     "sumac_kernel_launches": (C.c_longlong, []),
+    "sumac_gather_owned_rows": (i32, [p, i64, i64, p, i64, i32, p, p]),
     "sumac_relu_product_splits": (i32, [i64, i64, i32, i32]),
     "sumac_relu_product": (i32, [p, i64, p, p, p, p, i64, i64, i32, i32, p, p, p]),
     "sumac_relu_bat_c_workspace_bytes": (sz, [i64, i64, i32, i32]),

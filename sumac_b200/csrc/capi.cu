@@ -607,6 +607,17 @@ int sumac_sgd_step(float* p, float* g, float* buf, int64_t n, float lr, float mo
              reinterpret_cast<cudaStream_t>(stream));
   return launched("sgd_step");
 }
+int sumac_gather_owned_rows(const float* local, int64_t lo, int64_t hi, const int64_t* rows,
+                            int64_t nrows, int Dp, float* out, sumac_stream_t stream) {
+  if (nrows < 0 || hi < lo || padded(Dp) != Dp || (nrows > 0 && (!rows || !out)) ||
+      (nrows > 0 && hi > lo && !local))
+    return fail(SUMAC_ERR_ARG, "gather_owned_rows: bad args");
+  if (!aligned16(local) || !aligned16(out))
+    return fail(SUMAC_ERR_ARG, "gather_owned_rows: rows must be 16-byte aligned");
+  launch_gather_owned_rows(local, lo, hi, rows, nrows, Dp, out, reinterpret_cast<cudaStream_t>(stream));
+  return launched("gather_owned_rows");
+}
+
 int sumac_fill_zero(float* p, int64_t n, sumac_stream_t stream) {
   if (n < 0 || (n > 0 && !p)) return fail(SUMAC_ERR_ARG, "fill_zero: bad args");
   launch_fill_zero(p, n, reinterpret_cast<cudaStream_t>(stream));

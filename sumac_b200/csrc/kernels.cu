@@ -1168,4 +1168,33 @@ void launch_wait_flag(const int* flag, int* err, unsigned long long timeout_ns, 
   wait_flag_kernel<<<1, 1, 0, s>>>(flag, err, timeout_ns);
 }
 
+// ============================================================================================
+// Rows of a row-sharded factor: out[p] = local[rows[p] - lo] when this rank owns rows[p]
+// (lo <= rows[p] < hi), zero otherwise; one float4 per thread. An allreduce(sum) over the ranks
+// then completes the block rows exactly (one nonzero term per element).
+// ============================================================================================
+__global__ void gather_owned_rows_kernel(const float* __restrict__ local, int64_t lo, int64_t hi,
+                                         const int64_t* __restrict__ rows, int64_t nrows, int Dp,
+                                         float* __restrict__ out) {
+  const int q4 = Dp / 4;
+  const int64_t total = nrows * q4;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p = i / q4;
+    const int c4 = (int)(i - p * q4);
+    const int64_t r = rows[p];
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r >= lo && r < hi) v = reinterpret_cast<const float4*>(local + (r - lo) * Dp)[c4];
+    reinterpret_cast<float4*>(out)[i] = v;
+  }
+}
+
+void launch_gather_owned_rows(const float* local, int64_t lo, int64_t hi, const int64_t* rows,
+                              int64_t nrows, int Dp, float* out, cudaStream_t stream) {
+  if (nrows <= 0) return;
+  count_launch();
+  gather_owned_rows_kernel<<<grid_cap(nrows * (Dp / 4), 256, 148 * 4), 256, 0, stream>>>(
+      local, lo, hi, rows, nrows, Dp, out);
+}
+
 }  // namespace sb

@@ -62,6 +62,10 @@ void launch_salsa_prep(const float* Ffix, const int64_t* rows, int64_t b, int d,
                        void* scratch, unsigned int* counter, unsigned int* stats, int* err,
                        cudaStream_t stream);
 
+// out[p] = local[rows[p] - lo] if lo <= rows[p] < hi else 0 (Dp floats per row).
+void launch_gather_owned_rows(const float* local, int64_t lo, int64_t hi, const int64_t* rows,
+                              int64_t nrows, int Dp, float* out, cudaStream_t stream);
+
 // ---- finalize: sparse correction + update -------------------------------------------------
 enum FinalizeMode { FIN_STORE = 0, FIN_SALSA = 1, FIN_GRAD = 2 };
 struct FinalizeArgs {

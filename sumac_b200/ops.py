@@ -205,3 +205,11 @@ def wait_flag(flag, timeout_ns):
     dev = flag.device
     check(N.lib().sumac_wait_flag(ptr(flag), ptr(N.err_word(dev)), int(timeout_ns),
                                   N.stream_ptr(dev)), "wait_flag")
+
+
+def gather_owned_rows(local, lo, hi, rows, out):
+    """out[p] = F[rows[p]] for the rows [lo, hi) this rank holds as `local`, zero elsewhere."""
+    L = N.lib()
+    check(L.sumac_gather_owned_rows(ptr(local), int(lo), int(hi), ptr(rows), rows.numel(),
+                                    local.shape[1], ptr(out), N.stream_ptr(out.device)),
+          "gather_owned_rows")

@@ -49,9 +49,13 @@ def assemble_rows(local: Tensor, lo: int, hi: int, rows: Tensor, out: Tensor, gr
     F[lo:hi] as `local`: the rows this rank owns are written, the others are zero, and an
     allreduce(sum) completes the buffer on every rank (exact: one nonzero term per element).
     No host synchronisation, so it can be captured in a CUDA graph."""
-    idx = (rows - lo).clamp(0, max(hi - lo - 1, 0))
-    own = ((rows >= lo) & (rows < hi)).unsqueeze(1)
-    torch.where(own, local[idx], torch.zeros((), dtype=local.dtype, device=local.device), out=out)
+    if out.is_cuda:
+        ops.gather_owned_rows(local, lo, hi, rows, out)
+    else:  # the CPU (gloo) path of the host-logic tests
+        idx = (rows - lo).clamp(0, max(hi - lo - 1, 0))
+        own = ((rows >= lo) & (rows < hi)).unsqueeze(1)
+        torch.where(own, local[idx], torch.zeros((), dtype=local.dtype, device=local.device),
+                    out=out)
     dist.all_reduce(out, group=group)
 
 
