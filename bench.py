@@ -299,6 +299,7 @@ def run_ours(args):
     pk = peaks()
     tf32_peak = pk["bf16_tflops"] / 2.0
     tf32_measured = measure_tf32_matmul(dev) if rank == 0 else None
+    reduce_line = measure_reduce(dev, prec, tf32_peak) if rank == 0 else None
 
     # ---- e2e through the public API with host inputs
     e2e = None
@@ -348,6 +349,7 @@ def run_ours(args):
                      "frac": achieved / tf32_peak, "traffic": None,
                      "peak_source": f"{pk['source']} bf16 / 2 (dense TF32 rate)",
                      "tf32_matmul_measured_tflops": tf32_measured},
+        "fused_reduce": reduce_line,
         "e2e": e2e,
         "cpu_baseline": cpu,
         "clocks": clocks,
@@ -355,6 +357,45 @@ def run_ours(args):
     }
     print(json.dumps(line), flush=True)
     _teardown(st, world)
+
+
+def measure_reduce(dev, prec, tf32_peak):
+    """relu_bat_reduce (sum ReLU(A B^T), sum ReLU(A B^T)^2) at the reference's benchmark shapes
+    (kernel_benchmarks/relu_bat_reduce_bench.py:193-202: M=288768, N=1408, D in 16..256), flops
+    M N (2D-1) + 3 M N (:19-24), CUDA events over 20 launches of the C entry point."""
+    from sumac_b200 import _native
+    lib = _native.lib()
+    M, Nr = 288768, 1408
+    g = torch.Generator(device=dev).manual_seed(1)
+    P = _native.ptr
+    err = _native.err_word(dev)
+    stream = _native.stream_ptr(dev)
+    res = {"M": M, "N": Nr, "note": "operands L2-resident (the kernel is tensor / issue bound)"}
+    for D in (16, 32, 64, 128, 256):
+        A = torch.randn(M, D, device=dev, generator=g)
+        B = torch.randn(Nr, D, device=dev, generator=g)
+        out = torch.zeros(2, dtype=torch.float64, device=dev)
+        nb = lib.sumac_relu_bat_reduce_workspace_bytes(M, Nr, D, prec)
+        if nb == 0:
+            continue
+        ws = torch.empty(nb, dtype=torch.uint8, device=dev)
+
+        def launch():
+            _native.check(lib.sumac_relu_bat_reduce(P(A), P(B), M, Nr, D, P(out), prec, P(ws), nb,
+                                                    P(err), stream), "relu_bat_reduce")
+        for _ in range(3):
+            launch()
+        e0, e1 = torch.cuda.Event(True), torch.cuda.Event(True)
+        e0.record()
+        for _ in range(20):
+            launch()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / 20
+        tf = (M * Nr * (2 * D - 1) + 3 * M * Nr) / (ms * 1e-3) / 1e12
+        res[f"D{D}"] = {"ms": ms, "tflops": tf, "frac_tf32": tf / tf32_peak}
+    _native.raise_device_error(dev)
+    return res
 
 
 def _teardown(st, world):

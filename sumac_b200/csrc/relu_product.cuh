@@ -19,8 +19,8 @@
 //   warp 0       TMA producer: lane s < STAGES owns pipeline stage s (F chunk, C^T chunk),
 //                lane 16 + g owns X slot g. Copies issued by one thread complete one after
 //                another, copies from different lanes overlap.
-//   warp 1       first-MMA issuer (one thread): S = X_g F_c^T into the next of NBUF TMEM
-//                buffers (kind::tf32)
+//   warp 1, last first-MMA issuers (one thread each, even / odd pairs): S = X_g F_c^T into the
+//                next of NBUF TMEM buffers (kind::tf32)
 //   warps 2..9   epilogue, two warps per TMEM lane quadrant, each on half of the columns:
 //                tcgen05.ld S -> ReLU -> tcgen05.st R (or accumulate the sums); at the end of a
 //                group tcgen05.ld of each Y_g -> global
@@ -98,7 +98,13 @@ struct ProductCfg {
   // at least 120 KB so that only one CTA (and one 512-column TMEM allocation) lives on an SM
   static constexpr int SMEM_BYTES = SMEM_BYTES_RAW < 122880 ? 122880 : SMEM_BYTES_RAW;
   static_assert(SMEM_BYTES_RAW <= 232448, "shared memory budget");
-  static constexpr int NBUF = 3;                          // S buffers in TMEM
+  // S buffers in TMEM: as many as the 512 columns hold next to the Y accumulators (3xTF32
+  // product mode keeps a lo half per buffer), at most 8. More buffers in flight hide the round
+  // trip of a buffer (first MMA -> epilogue -> second MMA -> free), which bounds small ranks.
+  static constexpr int NBUF_FIT =
+      (512 - (REDUCE ? 0 : G * DP)) / (((X3 && !REDUCE) ? 2 : 1) * BN);
+  static constexpr int NBUF = NBUF_FIT < 8 ? NBUF_FIT : 8;
+  static_assert(NBUF >= 2, "at least two S buffers");
   static constexpr int TMEM_S_LO = NBUF * BN;             // lo halves of R (3xTF32)
   static constexpr int TMEM_Y = (X3 ? 2 : 1) * NBUF * BN; // G Y accumulators follow
   static_assert(REDUCE ? NBUF * BN <= 512 : TMEM_Y + G * DP <= 512, "TMEM budget");
@@ -113,7 +119,16 @@ struct ProductCfg {
   // product mode: second-MMA issuers, warp MMA2_WARP + i takes the tiles gi with gi % N2 == i
   static constexpr int MMA2_WARP = 11;
   static constexpr int N2 = 2;
-  static constexpr int THREADS = REDUCE ? 64 + EPI_THREADS + (AUX ? 32 : 0) : 32 * (11 + N2);
+  // first-MMA issuers: in TF32 reduce mode warp 1 takes the even pairs and warp MMA1B_WARP the
+  // odd ones (measured 15% faster at the reference's reduce shapes); elsewhere warp 1 alone (a
+  // second issuer gave no gain in product mode, and in 3xTF32 product mode at C4's shapes it
+  // ran into a bounded-wait timeout whose cause is not understood, so it is not used there)
+  static constexpr int N1 = (REDUCE && !X3) ? 2 : 1;
+  static constexpr int MMA1B_WARP = N1 == 2 ? 10 : 1;
+  static constexpr int THREADS =
+      REDUCE ? 32 * (N1 == 2 ? 11 : 10 + (AUX ? 1 : 0)) : 32 * (MMA2_WARP + N2);
+  // mbarriers, TMEM slot and abort flag sit below the epilogue's reduction scratch at +768 B
+  static_assert((3 * STAGES + 3 * NBUF + 5 * G + N1 + N2) * 8 + 8 <= 768, "barrier area");
   static constexpr int EPI_COLS = BN / 2;                 // S columns per epilogue warp
   static_assert(EPI_COLS % 16 == 0, "epilogue column split");
   static constexpr int LDW = EPI_COLS % 32 == 0 ? 32 : 16;  // tcgen05.ld/st width used
@@ -167,8 +182,8 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
   uint64_t* x_empty = x_ready + G;          // [G] last MMA reading the X slot completed
   uint64_t* y_full = x_empty + G;           // [G] Y accumulator complete
   uint64_t* y_empty = y_full + G;           // [G] Y accumulator read out
-  uint64_t* drain = y_empty + G;            // [1 + N2] each MMA thread's own MMAs completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1 + Cfg::N2);
+  uint64_t* drain = y_empty + G;            // [N1 + N2] each MMA thread's own MMAs completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + Cfg::N1 + Cfg::N2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   double* red = reinterpret_cast<double*>(smem + Cfg::SMEM_DATA + 768);  // [EPI_WARPS][2]
 
@@ -179,7 +194,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], REDUCE ? 1 : Cfg::N2);
+      mbar_init(&empty[s], REDUCE ? Cfg::N1 : Cfg::N2);
       mbar_init(&c16_ready[s], 32);
     }
     for (int b = 0; b < NBUF; ++b) {
@@ -190,11 +205,11 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
     for (int g = 0; g < G; ++g) {
       mbar_init(&x_full[g], 1);
       mbar_init(&x_ready[g], 32);
-      mbar_init(&x_empty[g], 1);
+      mbar_init(&x_empty[g], Cfg::N1);
       mbar_init(&y_full[g], 1);
       mbar_init(&y_empty[g], Cfg::EPI_THREADS);
     }
-    for (int i = 0; i <= Cfg::N2; ++i) mbar_init(&drain[i], 1);
+    for (int i = 0; i < Cfg::N1 + Cfg::N2; ++i) mbar_init(&drain[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -271,8 +286,11 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
         if (x_lane && xuses > 0) mbar_drain(&x_full[xslot], (xuses - 1) & 1);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == 1 || warp == Cfg::MMA1B_WARP) {
     // ------------------------------------------------------------------ first MMA (S = X F^T)
+    // issuer me1 takes the pairs with pair % N1 == me1; the stage and X-slot release barriers
+    // count one commit per issuer
+    const int me1 = warp == 1 ? 0 : 1;
     if (lane == 0) {
       const uint32_t sX_addr = smem_u32(sX);
       const uint32_t sSt_addr = smem_u32(sStage);
@@ -281,18 +299,20 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
       bool ok = true;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
         const WorkItem w = work_item(p, item);
+        // every issuer waits for all X slots of the group, even those it issues no pair on: the
+        // slots' release barrier (one commit per issuer) must not see a commit for this group
+        // before the previous group's phase has completed
+        for (int gi = 0; gi < w.ntiles && ok; ++gi)
+          if (!mbar_wait(X3 ? &x_ready[gi] : &x_full[gi], (slot_par >> gi) & 1u, abort_flag,
+                         p.err, DEV_TIMEOUT_X, p.timeout_ns)) ok = false;
         for (int c = w.c0; c < w.c1 && ok; ++c, ++chunk) {
           const int stage = chunk % STAGES;
           if (!mbar_wait(&full[stage], (chunk / STAGES) & 1, abort_flag, p.err, DEV_TIMEOUT_FULL,
                          p.timeout_ns)) { ok = false; break; }
           const uint32_t fbase = sSt_addr + stage * Cfg::STAGE_ALLOC;
           for (int gi = 0; gi < w.ntiles; ++gi, ++pair) {
+            if ((int)(pair % Cfg::N1) != me1) continue;
             const uint32_t buf = pair % NBUF;
-            if (c == w.c0 && !mbar_wait(X3 ? &x_ready[gi] : &x_full[gi], (slot_par >> gi) & 1u,
-                                        abort_flag, p.err, DEV_TIMEOUT_X, p.timeout_ns)) {
-              ok = false;
-              break;
-            }
             // the S buffer is free once the epilogue (reduce) or the second MMA (product) is
             // done with its previous use
             if (pair >= (uint32_t)NBUF &&
@@ -325,15 +345,17 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
               }
             }
             mma_commit(&s_full[buf]);
-            if (REDUCE && gi == w.ntiles - 1) mma_commit(&empty[stage]);
-            if (c == w.c1 - 1) mma_commit(&x_empty[gi]);  // last use of this X slot
           }
+          // reduce mode: the first MMAs are the stage's only readers
+          if (REDUCE && ok) mma_commit(&empty[stage]);
         }
+        if (ok)
+          for (int gi = 0; gi < w.ntiles; ++gi) mma_commit(&x_empty[gi]);  // X slots done
         slot_par ^= (1u << w.ntiles) - 1u;
       }
       // make sure every MMA this thread issued has completed before TMEM is released
-      mma_commit(&drain[0]);
-      mbar_drain(&drain[0], 0);
+      mma_commit(&drain[me1]);
+      mbar_drain(&drain[me1], 0);
     }
   } else if (!REDUCE && warp >= Cfg::MMA2_WARP && warp < Cfg::MMA2_WARP + Cfg::N2) {
     // ------------------------------------------------------------------ second MMA (Y += R C)
@@ -407,8 +429,8 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
         slot_par ^= mask;
         slot_used |= mask;
       }
-      mma_commit(&drain[1 + me]);
-      mbar_drain(&drain[1 + me], 0);
+      mma_commit(&drain[Cfg::N1 + me]);
+      mbar_drain(&drain[Cfg::N1 + me], 0);
     }
   } else if (warp >= 2 && warp < 2 + Cfg::EPI_WARPS) {
     // ------------------------------------------------------------------ epilogue (warps 2..9)
