@@ -181,3 +181,42 @@ def test_bounded_wait_reports_timeout_and_context_survives():
     assert _native.read_device_error(0) == 7
     x = torch.ones(4, device="cuda")
     assert float((x * 2).sum().item()) == 8.0
+
+
+def _relu_bat_c_fp64(A, B, C, chunk=20000):
+    """Y = ReLU(B A^T) C in float64 on the device, in row chunks (the oracle's formula)."""
+    A64, C64 = A.double(), C.double()
+    return torch.cat([torch.relu(B[i:i + chunk].double() @ A64.T) @ C64
+                      for i in range(0, B.shape[0], chunk)])
+
+
+@pytest.mark.parametrize("prec", PRECS)
+@pytest.mark.parametrize("D,N,M", [(16, 700, 140000), (32, 500, 80000)])
+def test_relu_bat_c_full_tile_groups(D, N, M, prec):
+    """Enough row tiles that every CTA holds a full group (8 tiles at d=16, 4 at d=32) and streams
+    the chunks once for the whole group: the schedule the C4 workload runs."""
+    g = torch.Generator(device="cuda").manual_seed(D + N)
+    A = torch.randn(N, D, device="cuda", generator=g)
+    B = torch.randn(M, D, device="cuda", generator=g)
+    C = torch.randn(N, D, device="cuda", generator=g)
+    Y = ops.relu_bat_c(A, B, C, prec)
+    _native.raise_device_error(0)
+    ref = _relu_bat_c_fp64(A, B, C)
+    assert float((Y.double() - ref).abs().max() / ref.abs().max()) < TOL[prec]
+
+
+@pytest.mark.parametrize("prec", PRECS)
+@pytest.mark.parametrize("D,N,M", [(16, 700, 160000), (32, 500, 80000)])
+def test_relu_bat_reduce_full_tile_groups(D, N, M, prec):
+    g = torch.Generator(device="cuda").manual_seed(D * 7 + N)
+    A = torch.randn(M, D, device="cuda", generator=g)
+    B = torch.randn(N, D, device="cuda", generator=g)
+    out = ops.relu_bat_reduce(A, B, prec)
+    _native.raise_device_error(0)
+    s1 = s2 = 0.0
+    for i in range(0, M, 20000):
+        R = torch.relu(A[i:i + 20000].double() @ B.double().T)
+        s1 += float(R.sum())
+        s2 += float((R * R).sum())
+    assert abs(float(out[0]) - s1) / s1 < TOL[prec]
+    assert abs(float(out[1]) - s2) / s2 < TOL[prec]
