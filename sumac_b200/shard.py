@@ -44,13 +44,45 @@ def split_direction(fixed: Tensor, out: Tensor, lo: int, hi: int) -> Tensor:
     return (out >= lo) & (out < hi)
 
 
-def assemble_rows(local: Tensor, lo: int, hi: int, rows: Tensor, out: Tensor, group=None) -> None:
+class SymmetricRows:
+    """A [rows, Dp] staging buffer in symmetric memory (every rank can load every other rank's
+    copy over NVLink), for the one-shot allreduce of assembled block rows: each rank reads its
+    peers' buffers directly, a few microseconds for ~90 KB instead of an NCCL ring."""
+
+    def __init__(self, rows: int, Dp: int, device, group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+        self.group_name = (group or dist.group.WORLD).group_name
+        self.buf = symm_mem.empty((rows, Dp), dtype=torch.float32, device=device)
+        symm_mem.rendezvous(self.buf, self.group_name)
+
+    def allreduce_into(self, b: int, out: Tensor) -> None:
+        torch.ops.symm_mem.one_shot_all_reduce_out(self.buf[:b], "sum", self.group_name, out)
+
+
+def make_symmetric_rows(rows: int, Dp: int, device, group=None):
+    """SymmetricRows on CUDA when symmetric memory is available, else None (NCCL allreduce)."""
+    if device.type != "cuda":
+        return None
+    try:
+        return SymmetricRows(rows, Dp, device, group)
+    except Exception:  # no peer access or no symmetric-memory backend: NCCL allreduce
+        return None
+
+
+def assemble_rows(local: Tensor, lo: int, hi: int, rows: Tensor, out: Tensor, group=None,
+                  sym: SymmetricRows | None = None) -> None:
     """out[p] = F[rows[p]] for a factor F row-sharded over the group, this rank holding
     F[lo:hi] as `local`: the rows this rank owns are written, the others are zero, and an
     allreduce(sum) completes the buffer on every rank (exact: one nonzero term per element).
-    No host synchronisation, so it can be captured in a CUDA graph."""
+    With `sym`, the rows are staged in symmetric memory and reduced by a one-shot allreduce;
+    otherwise by NCCL (or gloo on the CPU). No host synchronisation: graph-capturable."""
+    b = rows.numel()
     if out.is_cuda:
-        ops.gather_owned_rows(local, lo, hi, rows, out)
+        stage = sym.buf[:b] if sym is not None else out
+        ops.gather_owned_rows(local, lo, hi, rows, stage)
+        if sym is not None:
+            sym.allreduce_into(b, out)
+            return
     else:  # the CPU (gloo) path of the host-logic tests
         idx = (rows - lo).clamp(0, max(hi - lo - 1, 0))
         own = ((rows >= lo) & (rows < hi)).unsqueeze(1)
@@ -107,6 +139,8 @@ class ShardedSalsaState:
         self.FI_a = torch.zeros((self.dir_a.block_size, self.Dp), dtype=torch.float32, device=dev)
         self.ident = torch.arange(max(self.dir_a.block_size, self.dir_b.block_size),
                                   dtype=torch.int64, device=dev)
+        self.sym = make_symmetric_rows(max(self.dir_a.block_size, self.dir_b.block_size),
+                                       self.Dp, dev, group)
         self.momentum = float(cfg.momentum)
         self.lrate = float(np.float32(cfg.learning_rate))
         self.unbias = torch.empty(self.nb, dtype=torch.float32, device=dev)
@@ -158,14 +192,16 @@ class ShardedSalsaState:
             rows = self.dir_b.block_rows(perm_r, k)
             b = rows.numel()
             if b > 0:
-                assemble_rows(self.Ap, self.ra[0], self.ra[1], rows, self.FI_b[:b], self.group)
+                assemble_rows(self.Ap, self.ra[0], self.ra[1], rows, self.FI_b[:b], self.group,
+                              self.sym)
                 ops.salsa_block_update(self.FI_b, self.ident[:b], self.Bp, self.dB, self.d,
                                        self.dir_b.block_rowptr(k), self.dir_b.ent, self.momentum,
                                        self.lrate, self.unbias[k:k + 1], self.prec, self.ws_b)
             rows = self.dir_a.block_rows(perm_c, k)
             b = rows.numel()
             if b > 0:
-                assemble_rows(self.Bp, self.rb[0], self.rb[1], rows, self.FI_a[:b], self.group)
+                assemble_rows(self.Bp, self.rb[0], self.rb[1], rows, self.FI_a[:b], self.group,
+                              self.sym)
                 ops.salsa_block_update(self.FI_a, self.ident[:b], self.Ap, self.dA, self.d,
                                        self.dir_a.block_rowptr(k), self.dir_a.ent, self.momentum,
                                        self.lrate, self.unbias[k:k + 1], self.prec, self.ws_a)
