@@ -84,6 +84,79 @@ def _rows_csr(S_index, S_value, perm, m):
     return rowptr, ent
 
 
+class GDState:
+    """Device state of one GD run: padded factors and gradients, the optimizer, the fixed block
+    partition with both CSR views of S, and the evaluation accumulators."""
+
+    def __init__(self, S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfig,
+                 A: Tensor, B: Tensor, gen_blocks, gen_loader):
+        dev = cfg.device
+        self.cfg = cfg
+        self.d = d = cfg.rank
+        self.Dp = Dp = ops.padded_rank(d)
+        self.prec = cfg.precision()
+        self.Ap = ops.pad_factor(A.detach().to(torch.float32), Dp)
+        self.Bp = ops.pad_factor(B.detach().to(torch.float32), Dp)
+        self.gA = torch.zeros_like(self.Ap)
+        self.gB = torch.zeros_like(self.Bp)
+        self.opt = _Optimizer(cfg, [self.Ap, self.Bp], [self.gA, self.gB], d)
+        nb = cfg.num_blocks
+        perm = draw_perm(m, gen_blocks, dev)     # one partition for the whole run (datasets.py:34)
+        bs = (m + nb - 1) // nb
+        self.dir_b = SparseDirection(S_index[0], S_index[1], S_value, m, n, nb)
+        self.dir_b.rebuild(perm)                 # by column j, entries {local row, S}
+        rowptr_pos, self.ent_pos = _rows_csr(S_index, S_value, perm, m)
+        self.blocks = []
+        for k in range(nb):
+            rows = perm[k * bs:min(m, (k + 1) * bs)]
+            self.blocks.append((rows, self.dir_b.block_rowptr(k),
+                                rowptr_pos[k * bs:k * bs + rows.numel() + 1]))
+        self.loader = DataLoader(list(range(nb)), batch_size=cfg.batch_blocks,
+                                 shuffle=cfg.shuffle_blocks, collate_fn=lambda b: b,
+                                 generator=gen_loader)
+        self.sum_v = float(S_value.double().sum().item())
+        self.s_norm = float(torch.linalg.norm(S_value.double()).item())
+        self.terms = torch.zeros(8, dtype=torch.float64, device=dev)
+
+    def epoch(self, report: bool) -> None:
+        """One pass over the blocks in loader order (training/gd.py:160-204): per batch the loss
+        terms (report epochs, before the step), the block gradients, one optimizer step."""
+        d, prec = self.d, self.prec
+        Ap, Bp, gA, gB = self.Ap, self.Bp, self.gA, self.gB
+        if report:
+            self.terms.zero_()
+        for batch in self.loader:
+            if report:
+                for k in batch:
+                    rows, rp_b, _ = self.blocks[k]
+                    if rows.numel() > 0:
+                        ops.block_loss_terms(Ap, Bp, d, rows, rp_b, self.dir_b.ent, self.terms, 1,
+                                             prec)
+            ops.fill_zero(gA)
+            first = True
+            for k in batch:
+                rows, rp_b, rp_a = self.blocks[k]
+                if rows.numel() == 0:
+                    continue
+                ops.gd_block_grad(Ap, Bp, d, rows, rp_b, self.dir_b.ent, rp_a, self.ent_pos, gA,
+                                  gB, 0 if first else 1, prec)
+                first = False
+            if first:
+                ops.fill_zero(gB)
+            self.opt.step()
+
+    def report_metrics(self) -> tuple[float, float, float]:
+        """(rmse, jacc, cost) of the epoch's accumulated loss terms (eval.py:57-108)."""
+        t = self.terms.cpu().tolist()
+        sum_sr, sum_sr2, obs_sq, res_m, res_l, jnum = t[:6]
+        total_errz = sum_sr2 - obs_sq + res_l
+        total_mse = sum_sr2 - obs_sq + res_m
+        jacc = 1.0 - jnum / (self.sum_v + sum_sr - jnum)
+        rmse = math.sqrt(max(total_mse, 0.0)) / (self.s_norm + 1e-16)
+        errZ = math.sqrt(max(total_errz, 0.0)) / (self.s_norm + 1e-16)
+        return rmse, jacc, errZ
+
+
 def GD_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfig,
             A_init: Tensor | None = None, B_init: Tensor | None = None):
     assert cfg.num_blocks is not None and cfg.device is not None
@@ -96,68 +169,19 @@ def GD_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfig,
         A, B = init_salsa_factors(S_index, S_value, m, n, d, gen)
     else:
         A, B = A_init.to(dev).clone(), B_init.to(dev).clone()
-    Dp = ops.padded_rank(d)
-    prec = cfg.precision()
-    Ap = ops.pad_factor(A.detach().to(torch.float32), Dp)
-    Bp = ops.pad_factor(B.detach().to(torch.float32), Dp)
-    gA = torch.zeros_like(Ap)
-    gB = torch.zeros_like(Bp)
-    opt = _Optimizer(cfg, [Ap, Bp], [gA, gB], d)
-
-    nb = cfg.num_blocks
-    perm = draw_perm(m, gen_blocks, dev)       # one partition for the whole run (datasets.py:34)
-    bs = (m + nb - 1) // nb
-    dir_b = SparseDirection(S_index[0], S_index[1], S_value, m, n, nb)
-    dir_b.rebuild(perm)                        # by column j, entries {local row, S}
-    rowptr_pos, ent_pos = _rows_csr(S_index, S_value, perm, m)
-    blocks = []
-    for k in range(nb):
-        rows = perm[k * bs:min(m, (k + 1) * bs)]
-        blocks.append((rows, dir_b.block_rowptr(k), rowptr_pos[k * bs:k * bs + rows.numel() + 1]))
-    loader = DataLoader(list(range(nb)), batch_size=cfg.batch_blocks, shuffle=cfg.shuffle_blocks,
-                        collate_fn=lambda b: b, generator=gen_loader)
-    evaluator = Evaluator(S_index, S_value, d, prec)
-    sum_v = float(S_value.double().sum().item())
-    s_norm = float(torch.linalg.norm(S_value.double()).item())
-
-    rmse, jacc, errZ = evaluator(Ap, Bp)
+    st = GDState(S_index, S_value, m, n, cfg, A, B, gen_blocks, gen_loader)
+    evaluator = Evaluator(S_index, S_value, d, st.prec)
+    rmse, jacc, errZ = evaluator(st.Ap, st.Bp)
     if cfg.verbose:
         print(f"[epoch 0/{cfg.max_iterations}]: cost = {errZ:.6f}, rmse = {rmse:.6f}, "
               f"jacc = {jacc:.6f}, time = 0.0000s")
     hist = {"cost": [], "rmse": [], "jacc": [], "time": []}
-    terms = torch.zeros(8, dtype=torch.float64, device=dev)
     t0 = time.time()
     for epoch in range(1, cfg.max_iterations + 1):
         report = epoch % cfg.eval_interval == 0
+        st.epoch(report)
         if report:
-            terms.zero_()
-        for batch in loader:
-            for i, k in enumerate(batch):
-                rows, rp_b, rp_a = blocks[k]
-                if rows.numel() == 0:
-                    continue
-                if report:
-                    ops.block_loss_terms(Ap, Bp, d, rows, rp_b, dir_b.ent, terms, 1, prec)
-            ops.fill_zero(gA)
-            first = True
-            for k in batch:
-                rows, rp_b, rp_a = blocks[k]
-                if rows.numel() == 0:
-                    continue
-                ops.gd_block_grad(Ap, Bp, d, rows, rp_b, dir_b.ent, rp_a, ent_pos, gA, gB,
-                                  0 if first else 1, prec)
-                first = False
-            if first:
-                ops.fill_zero(gB)
-            opt.step()
-        if report:
-            t = terms.cpu().tolist()
-            sum_sr, sum_sr2, obs_sq, res_m, res_l, jnum = t[:6]
-            total_errz = sum_sr2 - obs_sq + res_l
-            total_mse = sum_sr2 - obs_sq + res_m
-            jacc = 1.0 - jnum / (sum_v + sum_sr - jnum)
-            rmse = math.sqrt(max(total_mse, 0.0)) / (s_norm + 1e-16)
-            errZ = math.sqrt(max(total_errz, 0.0)) / (s_norm + 1e-16)
+            rmse, jacc, errZ = st.report_metrics()
             elapsed = time.time() - t0
             hist["cost"].append(errZ)
             hist["rmse"].append(rmse)
@@ -170,7 +194,7 @@ def GD_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfig,
     total = time.time() - t0
     if cfg.verbose:
         print(f"\nTotal elapsed time: {total:.2f} sec")
-    rmse, jacc, errZ = evaluator(Ap, Bp)
+    rmse, jacc, errZ = evaluator(st.Ap, st.Bp)
     if cfg.verbose:
         print(f"EVAL: cost={errZ:.6f}, rmse={rmse:.6f}, jacc={jacc:.6f}, time={total:.4f}s")
-    return Ap[:, :d].contiguous(), Bp[:, :d].contiguous(), hist
+    return st.Ap[:, :st.d].contiguous(), st.Bp[:, :st.d].contiguous(), hist
