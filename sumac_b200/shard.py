@@ -256,3 +256,168 @@ def sharded_salsa_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: Su
     _native.raise_device_error(dev)
     A, B = st.factors()
     return A, B, hist
+
+
+# ---------------------------------------------------------------------------------------------
+# GD (training/gd.py:110-253): every step's row block is split over the ranks
+# ---------------------------------------------------------------------------------------------
+def subblock_bounds(m: int, nb: int, k: int, rank: int, world: int) -> tuple[int, int]:
+    """Positions [lo, hi) (within block k of the fixed partition) of this rank's sub-block."""
+    bs = (m + nb - 1) // nb
+    bk = max(0, min(bs, m - k * bs))
+    return bk * rank // world, bk * (rank + 1) // world
+
+
+def virtual_positions(pos: Tensor, m: int, nb: int, rank: int, world: int) -> Tensor:
+    """For global positions `pos` in the partition permutation: the rank-local virtual position
+    k * bsub + (t - lo_k) when the position falls in this rank's sub-block of its block k
+    (t = pos - k * bs), else -1. Sub-blocks occupy whole virtual blocks of bsub = ceil(bs / world)
+    slots, so the single-GPU per-block CSR builder (block = vpos / bsub) works unchanged."""
+    bs = (m + nb - 1) // nb
+    bsub = (bs + world - 1) // world
+    k = torch.div(pos, bs, rounding_mode="floor")
+    t = pos - k * bs
+    bk = torch.clamp(m - k * bs, max=bs)
+    lo = torch.div(bk * rank, world, rounding_mode="floor")
+    hi = torch.div(bk * (rank + 1), world, rounding_mode="floor")
+    own = (t >= lo) & (t < hi)
+    return torch.where(own, k * bsub + (t - lo), torch.full_like(pos, -1))
+
+
+class ShardedGDState:
+    """One rank of a GD run whose row blocks are split over the ranks. The factors, their
+    gradients and the optimizer state are replicated; each rank computes the gradients of its
+    sub-block (its rows of grad A, a partial grad B), grad B is allreduced (sum) and the block's
+    rows of grad A are completed by an exact allreduce, then every rank takes the same optimizer
+    step. Same partition, loader order and optimizer as GDState."""
+
+    def __init__(self, S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfig,
+                 A: Tensor, B: Tensor, gen_blocks, gen_loader, group=None):
+        from torch.utils.data import DataLoader
+        from .gd import _Optimizer
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        dev = cfg.device
+        self.cfg = cfg
+        self.d = d = cfg.rank
+        self.Dp = Dp = ops.padded_rank(d)
+        self.prec = cfg.precision()
+        self.Ap = ops.pad_factor(A.detach().to(torch.float32), Dp)
+        self.Bp = ops.pad_factor(B.detach().to(torch.float32), Dp)
+        self.gA = torch.zeros_like(self.Ap)
+        self.gB = torch.zeros_like(self.Bp)
+        self.opt = _Optimizer(cfg, [self.Ap, self.Bp], [self.gA, self.gB], d)
+        self.m, self.n = m, n
+        nb = self.nb = cfg.num_blocks
+        perm = draw_perm(m, gen_blocks, dev)     # the same partition on every rank
+        bs = (m + nb - 1) // nb
+        bsub = (bs + self.world - 1) // self.world
+        nv = nb * bsub
+        perm_inv = torch.empty_like(perm)
+        perm_inv[perm] = torch.arange(m, device=dev)
+        vpos = virtual_positions(perm_inv[S_index[0]], m, nb, self.rank, self.world)
+        keep = vpos >= 0
+        vp, cols, vals = vpos[keep], S_index[1][keep], S_value[keep]
+        # by column j (entries {row within the sub-block, S}): the CSR builder on the identity
+        # permutation of the virtual positions
+        self.dir_b = SparseDirection(vp, cols, vals, nv, n, nb)
+        self.dir_b.rebuild(torch.arange(nv, dtype=torch.int64, device=dev))
+        # by row within the sub-block (entries {j, S}), in the support's original order
+        order = torch.sort(vp, stable=True).indices
+        self.rowptr_v = torch.searchsorted(vp[order], torch.arange(nv + 1, device=dev)).to(torch.int32)
+        self.ent_v = torch.stack([cols[order].to(torch.int32),
+                                  vals[order].to(torch.float32).view(torch.int32)], 1).contiguous()
+        self.blocks = []
+        for k in range(nb):
+            lo, hi = subblock_bounds(m, nb, k, self.rank, self.world)
+            full = perm[k * bs:min(m, (k + 1) * bs)]
+            self.blocks.append((full[lo:hi], full, self.dir_b.block_rowptr(k),
+                                self.rowptr_v[k * bsub:k * bsub + (hi - lo) + 1]))
+        self.gbuf = torch.zeros((bs, Dp), dtype=torch.float32, device=dev)
+        self.loader = DataLoader(list(range(nb)), batch_size=cfg.batch_blocks,
+                                 shuffle=cfg.shuffle_blocks, collate_fn=lambda b: b,
+                                 generator=gen_loader)
+        self.sum_v = float(S_value.double().sum().item())
+        self.s_norm = float(torch.linalg.norm(S_value.double()).item())
+        self.terms = torch.zeros(8, dtype=torch.float64, device=dev)
+
+    def epoch(self, report: bool) -> None:
+        d, prec = self.d, self.prec
+        Ap, Bp, gA, gB = self.Ap, self.Bp, self.gA, self.gB
+        if report:
+            self.terms.zero_()
+        for batch in self.loader:
+            if report:
+                for k in batch:
+                    sub, _, rp_b, _ = self.blocks[k]
+                    if sub.numel() > 0:
+                        ops.block_loss_terms(Ap, Bp, d, sub, rp_b, self.dir_b.ent, self.terms, 1,
+                                             prec)
+            ops.fill_zero(gA)
+            first = True
+            for k in batch:
+                sub, _, rp_b, rp_a = self.blocks[k]
+                if sub.numel() == 0:
+                    continue
+                ops.gd_block_grad(Ap, Bp, d, sub, rp_b, self.dir_b.ent, rp_a, self.ent_v, gA, gB,
+                                  0 if first else 1, prec)
+                first = False
+            if first:
+                ops.fill_zero(gB)
+            dist.all_reduce(gB, group=self.group)
+            for k in batch:  # the block's rows of grad A: disjoint per rank, zero elsewhere
+                full = self.blocks[k][1]
+                b = full.numel()
+                if b == 0:
+                    continue
+                torch.index_select(gA, 0, full, out=self.gbuf[:b])
+                dist.all_reduce(self.gbuf[:b], group=self.group)
+                gA.index_copy_(0, full, self.gbuf[:b])
+            self.opt.step()
+        if report:
+            dist.all_reduce(self.terms, group=self.group)
+
+    def report_metrics(self) -> tuple[float, float, float]:
+        from .gd import GDState
+        return GDState.report_metrics(self)
+
+
+def sharded_gd_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfig,
+                    A_init: Tensor | None = None, B_init: Tensor | None = None, group=None):
+    """GD_loop with every step's row block split over the process group; same schedule,
+    generators and history; every rank returns the whole factors."""
+    assert cfg.num_blocks is not None and cfg.device is not None
+    dev = cfg.device
+    gen, gen_blocks, gen_loader = cfg.get_generator()
+    S_index = S_index.to(dev)
+    S_value = S_value.to(dev)
+    d = cfg.rank
+    if A_init is None or B_init is None:
+        A, B = init_salsa_factors(S_index, S_value, m, n, d, gen)
+    else:
+        A, B = A_init.to(dev).clone(), B_init.to(dev).clone()
+    st = ShardedGDState(S_index, S_value, m, n, cfg, A, B, gen_blocks, gen_loader, group)
+    evaluator = Evaluator(S_index, S_value, d, st.prec)
+    rmse, jacc, errZ = evaluator(st.Ap, st.Bp)
+    verbose = cfg.verbose and st.rank == 0
+    if verbose:
+        print(f"[epoch 0/{cfg.max_iterations}]: cost = {errZ:.6f}, rmse = {rmse:.6f}, "
+              f"jacc = {jacc:.6f}, time = 0.0000s")
+    hist = {"cost": [], "rmse": [], "jacc": [], "time": []}
+    t0 = time.time()
+    for epoch in range(1, cfg.max_iterations + 1):
+        report = epoch % cfg.eval_interval == 0
+        st.epoch(report)
+        if report:
+            rmse, jacc, errZ = st.report_metrics()
+            elapsed = time.time() - t0
+            hist["cost"].append(errZ)
+            hist["rmse"].append(rmse)
+            hist["jacc"].append(jacc)
+            hist["time"].append(elapsed)
+            if verbose:
+                print(f"[epoch {epoch}/{cfg.max_iterations}]: cost = {errZ:.6f}, "
+                      f"rmse = {rmse:.6f}, jacc = {jacc:.6f}, time = {elapsed:.4f}s")
+    _native.raise_device_error(dev)
+    return st.Ap[:, :d].contiguous(), st.Bp[:, :d].contiguous(), hist

@@ -92,7 +92,13 @@ def sumac_factorize(*, S_index: Tensor, S_value: Tensor, shape: tuple[int, int],
                 B_init = B_init[col_mask]
         config.print_prefactor_report(S_value, m, n, torch.cuda.device_count())
         if config.method == SumacMethod.GD:
-            A, B, costs = GD_loop(S_index, S_value, m_eff, n_eff, config, A_init, B_init)
+            if _world_size() > 1:
+                # one process per GPU: every step's row block split over the process group
+                from .shard import sharded_gd_loop
+                A, B, costs = sharded_gd_loop(S_index, S_value, m_eff, n_eff, config, A_init,
+                                              B_init)
+            else:
+                A, B, costs = GD_loop(S_index, S_value, m_eff, n_eff, config, A_init, B_init)
         elif config.method == SumacMethod.SALSA:
             if _world_size() > 1:
                 # one process per GPU: rows of A and B sharded over the default process group

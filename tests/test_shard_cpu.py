@@ -74,3 +74,25 @@ def test_assemble_and_gather_two_gloo_ranks():
         p.join(timeout=60)
     for rank, a, b in res:
         assert a is True and b is True, (rank, a, b)
+
+
+def test_gd_subblocks_partition_every_position_once():
+    from sumac_b200.shard import subblock_bounds, virtual_positions
+    for m, nb, world in [(1000, 7, 2), (8131 * 3 + 5, 4, 8), (50, 10, 3), (97, 1, 4)]:
+        bs = (m + nb - 1) // nb
+        bsub = (bs + world - 1) // world
+        pos = torch.arange(m)
+        owner = torch.full((m,), -1)
+        for r in range(world):
+            v = virtual_positions(pos, m, nb, r, world)
+            own = v >= 0
+            assert torch.all(owner[own] == -1)
+            owner[own] = r
+            vv = v[own]
+            assert vv.unique().numel() == vv.numel() and int(vv.max()) < nb * bsub
+            # a position keeps its block, and its slot within the sub-block
+            k = pos[own] // bs
+            assert torch.equal(vv // bsub, k)
+            lo = torch.tensor([subblock_bounds(m, nb, int(kk), r, world)[0] for kk in k])
+            assert torch.equal(vv % bsub, pos[own] - k * bs - lo)
+        assert torch.all(owner >= 0)

@@ -1,6 +1,6 @@
-"""Row-sharded SALSA on two GPUs (two NCCL ranks, sumac_b200/shard.py) against the reference's
-own SALSA run (tests/golden/e2e_salsa.npz): the same factors and history as the single-GPU path.
-Skipped when fewer than two GPUs are visible."""
+"""Sharded solvers on two GPUs (two NCCL ranks, sumac_b200/shard.py) against the reference's own
+runs (tests/golden/e2e_salsa.npz, e2e_gd.npz): the same factors and history as the single-GPU
+paths. Skipped when fewer than two GPUs are visible."""
 import os
 import socket
 
@@ -21,7 +21,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, method="salsa"):
     try:
         import torch.distributed as dist
         from sumac_b200 import SumacConfig, SumacMethod, sumac_factorize
@@ -31,11 +31,14 @@ def _worker(rank, world, port, q):
         torch.cuda.set_device(rank)
         dist.init_process_group("nccl", rank=rank, world_size=world,
                                 device_id=torch.device("cuda", rank))
-        g = load_golden("e2e_salsa")
-        cfg = SumacConfig(method=SumacMethod.SALSA, rank=int(g["rank"]),
-                          max_iterations=int(g["iters"]), num_blocks=int(g["num_blocks"]),
-                          seed=int(g["seed"]), learning_rate=float(g["lr"]), verbose=False,
-                          perm_device="cpu", eval_interval=1, device=f"cuda:{rank}")
+        g = load_golden("e2e_" + method)
+        extra = (dict(eval_interval=1) if method == "salsa" else
+                 dict(eval_interval=2, batch_blocks=int(g["batch_blocks"]), shuffle_blocks=True))
+        cfg = SumacConfig(method=SumacMethod.SALSA if method == "salsa" else SumacMethod.GD,
+                          rank=int(g["rank"]), max_iterations=int(g["iters"]),
+                          num_blocks=int(g["num_blocks"]), seed=int(g["seed"]),
+                          learning_rate=float(g["lr"]), verbose=False, perm_device="cpu",
+                          device=f"cuda:{rank}", **extra)
         dev = torch.device("cuda", rank)
         A, B, hist = sumac_factorize(S_index=torch.from_numpy(g["S_index"]).to(dev),
                                      S_value=torch.from_numpy(g["S_value"]).to(dev),
@@ -49,18 +52,19 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_sharded_salsa_matches_reference_run():
+@pytest.mark.parametrize("method", ["salsa", "gd"])
+def test_sharded_solver_matches_reference_run(method):
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, method)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(world)]
     for p in procs:
         p.join(timeout=60)
-    g = load_golden("e2e_salsa")
+    g = load_golden("e2e_" + method)
     for rank, A, B, hist, err in res:
         assert err is None, (rank, err)
         assert rel_err(A, g["A"]) < 1e-4
