@@ -491,13 +491,11 @@ def run_gd(args):
     from sumac_b200.gd import GDState
     from sumac_b200.salsa import init_salsa_factors
     rank, world, local = dist_info()
-    if world > 1:
-        if rank == 0:
-            print(json.dumps({"metric": "GD epochs/s", "unavailable":
-                              "the GD solver is not sharded over GPUs yet (SALSA is)"}))
-        return
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
     cfgd = CONFIGS[args.config]
     idx_np, val_np, shape = MAKERS[args.config]()
     d, nb = cfgd["rank"], cfgd["num_blocks"]
@@ -509,12 +507,18 @@ def run_gd(args):
                       allow_tf32=args.precision == "tf32", device=dev)
     gen, gen_blocks, gen_loader = cfg.get_generator()
     A, B = init_salsa_factors(S_index, S_value, m, n, d, gen)
-    st = GDState(S_index, S_value, m, n, cfg, A, B, gen_blocks, gen_loader)
+    if world > 1:
+        from sumac_b200.shard import ShardedGDState
+        st = ShardedGDState(S_index, S_value, m, n, cfg, A, B, gen_blocks, gen_loader)
+    else:
+        st = GDState(S_index, S_value, m, n, cfg, A, B, gen_blocks, gen_loader)
     del A, B
     for _ in range(args.warmup):
         st.epoch(False)
     torch.cuda.synchronize()
     _native.raise_device_error(dev)
+    if world > 1:
+        dist.barrier()
     lib = _native.lib()
     launches0 = lib.sumac_kernel_launches()
     ev0, ev1 = torch.cuda.Event(True), torch.cuda.Event(True)
@@ -526,18 +530,30 @@ def run_gd(args):
         torch.cuda.synchronize()
     _native.raise_device_error(dev)
     ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    launches = lib.sumac_kernel_launches() - launches0
+    if rank != 0:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     flops = 6.0 * m * n * d
     tf = flops / (ms * 1e-3) / 1e12
     pk = peaks()
     tf32_peak = pk["bf16_tflops"] / 2.0
     print(json.dumps({
-        "metric": "GD epochs/s (C5)", "value": 1e3 / ms, "unit": "epoch/s", "n_gpus": 1,
+        "metric": "GD epochs/s (C5)", "value": 1e3 / ms, "unit": "epoch/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None,
         "dtype": "tf32" if args.precision == "tf32" else "f32 (3xTF32)",
         "data": "synthetic (seeded stand-in)",
         "config": {"workload": cfgd["desc"], "m_eff": m, "n_eff": n, "nnz": int(val_np.size),
-                   "rank": d, "num_blocks": nb, "method": "GD", "parallelism": "single GPU",
+                   "rank": d, "num_blocks": nb, "method": "GD",
+                   "parallelism": "single GPU" if world == 1 else
+                   f"each step's row block split over {world} GPUs (NCCL allreduce of grad B)",
                    "l2": "inputs larger than L2 (factors 256 MB each, CSR 3.2 GB)"},
         "roofline": {"bound": "tensor", "achieved": tf, "peak": tf32_peak, "unit": "TFLOP/s",
                      "frac": tf / tf32_peak, "traffic": None,
@@ -546,8 +562,11 @@ def run_gd(args):
         "cpu_baseline": None, "cpu_note": "not run on CPU: C5 does not fit the host's dense "
                                           "fallbacks (a 32 GB block product in fp32)",
         "e2e": None, "clocks": clk.summary(),
-        "gpu_launches": int(lib.sumac_kernel_launches() - launches0),
+        "gpu_launches": int(launches),
     }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_product_only(args):
