@@ -146,15 +146,19 @@ class GDState:
             self.opt.step()
 
     def report_metrics(self) -> tuple[float, float, float]:
-        """(rmse, jacc, cost) of the epoch's accumulated loss terms (eval.py:57-108)."""
-        t = self.terms.cpu().tolist()
-        sum_sr, sum_sr2, obs_sq, res_m, res_l, jnum = t[:6]
-        total_errz = sum_sr2 - obs_sq + res_l
-        total_mse = sum_sr2 - obs_sq + res_m
-        jacc = 1.0 - jnum / (self.sum_v + sum_sr - jnum)
-        rmse = math.sqrt(max(total_mse, 0.0)) / (self.s_norm + 1e-16)
-        errZ = math.sqrt(max(total_errz, 0.0)) / (self.s_norm + 1e-16)
-        return rmse, jacc, errZ
+        return gd_epoch_metrics(self.terms, self.sum_v, self.s_norm)
+
+
+def gd_epoch_metrics(terms: Tensor, sum_v: float, s_norm: float) -> tuple[float, float, float]:
+    """(rmse, jacc, cost) of an epoch's accumulated block loss terms (eval.py:57-108)."""
+    t = terms.cpu().tolist()
+    sum_sr, sum_sr2, obs_sq, res_m, res_l, jnum = t[:6]
+    total_errz = sum_sr2 - obs_sq + res_l
+    total_mse = sum_sr2 - obs_sq + res_m
+    jacc = 1.0 - jnum / (sum_v + sum_sr - jnum)
+    rmse = math.sqrt(max(total_mse, 0.0)) / (s_norm + 1e-16)
+    errZ = math.sqrt(max(total_errz, 0.0)) / (s_norm + 1e-16)
+    return rmse, jacc, errZ
 
 
 def GD_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfig,

@@ -379,8 +379,8 @@ class ShardedGDState:
             dist.all_reduce(self.terms, group=self.group)
 
     def report_metrics(self) -> tuple[float, float, float]:
-        from .gd import GDState
-        return GDState.report_metrics(self)
+        from .gd import gd_epoch_metrics
+        return gd_epoch_metrics(self.terms, self.sum_v, self.s_norm)
 
 
 def sharded_gd_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfig,
