@@ -485,7 +485,7 @@ def run_reference(args):
 def run_gd(args):
     """GD epochs per second on one GPU with the data resident (C5): each step is one pass over
     the 123 row blocks (block gradients through the fused product passes, one Adam step per
-    block). Algorithmic work 6 m n d per epoch (L, grad A, grad B; SURVEY 8(d))."""
+    block). Algorithmic work 6 m n d per epoch (L, grad A, grad B)."""
     from sumac_b200 import SumacConfig, SumacMethod, _native
     from sumac_b200.data import prune_zero_rows_cols
     from sumac_b200.gd import GDState

@@ -17,7 +17,9 @@ import os
 import sys
 
 os.environ.setdefault("TORCHDYNAMO_DISABLE", "1")
-sys.path.insert(0, os.environ.get("SUMAC_REFERENCE_SRC", "/root/reference/src"))
+if "SUMAC_REFERENCE_SRC" not in os.environ:
+    sys.exit("set SUMAC_REFERENCE_SRC to the reference's src directory (see the docstring)")
+sys.path.insert(0, os.environ["SUMAC_REFERENCE_SRC"])
 
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
