@@ -539,7 +539,8 @@ __device__ __forceinline__ float support_coef(int mode, float val, float L) {
 }
 
 template <int DP>
-__global__ void finalize_kernel(FinalizeArgs a) {
+// 64 registers (4 CTAs of 256 threads per SM): the pass is latency-bound, warps in flight matter
+__global__ void __launch_bounds__(256, 4) finalize_kernel(FinalizeArgs a) {
   constexpr int G = DP / 4 < 32 ? DP / 4 : 32;  // lanes per row
   constexpr int V = DP / 4 / G;                  // float4 slices per lane
   constexpr int RPW = 32 / G;                    // rows per warp
