@@ -64,13 +64,21 @@ def sumac_factorize(*, S_index: Tensor, S_value: Tensor, shape: tuple[int, int],
     from .gd import GD_loop
     from .salsa import salsa_loop
 
-    m, n = validate_sumac_inputs(S_index=S_index, S_value=S_value, shape=shape, A_init=A_init,
+    S_index_w, S_value_w = S_index, S_value
+    if (torch.cuda.is_available() and isinstance(S_index, Tensor) and isinstance(S_value, Tensor)):
+        # the data checks (finite, ranges, duplicates: a unique over nnz keys) and the pruning run
+        # on the GPU the factorisation will use; the inputs are copied there once
+        target = _cuda_device(resolve_sumac_device(S_index, S_value, config))
+        S_index_w = S_index.to(target, non_blocking=True)
+        S_value_w = S_value.to(target, non_blocking=True)
+    m, n = validate_sumac_inputs(S_index=S_index_w, S_value=S_value_w, shape=shape, A_init=A_init,
                                  B_init=B_init, config=config)
     if config.dtype != torch.float32:
         raise NotImplementedError("sumac_b200 computes in float32 (TF32 / 3xTF32 tensor cores); "
                                   "dtype=torch.float64 is not supported")
     with _matmul_precision(config.allow_tf32):
         requested = resolve_sumac_device(S_index, S_value, config)
+        S_index, S_value = S_index_w, S_value_w
         # pruning and block sizing are integer work on the input's device, before the GPU is needed
         S_index = S_index.to(S_value.device) if S_index.device != S_value.device else S_index
         S_index, row_mask, col_mask, m_eff, n_eff = prune_zero_rows_cols(S_index, shape=(m, n))
