@@ -16,9 +16,9 @@
 // and one chunk) run chunk-major: (c0, tile 0), (c0, tile 1), ..., (c1 - 1, last tile). Each
 // tile has its own Y accumulator in TMEM (G x Dp columns), next to NBUF S buffers.
 //
-//   warp 0       TMA producer: lane s < STAGES owns pipeline stage s (F chunk, C^T chunk),
-//                lane 16 + g owns X slot g. Copies issued by one thread complete one after
-//                another, copies from different lanes overlap.
+//   warp 0       TMA producer: lanes 0..15 fill each stage (F chunk, C^T chunk) together, one
+//                copy per lane; lane 16 + g owns X slot g. Copies issued by one thread complete
+//                one after another, copies from different lanes overlap.
 //   warp 1, last first-MMA issuers (one thread each, even / odd pairs): S = X_g F_c^T into the
 //                next of NBUF TMEM buffers (kind::tf32)
 //   warps 2..9   epilogue, two warps per TMEM lane quadrant, each on half of the columns:
@@ -77,7 +77,7 @@ struct ProductCfg {
   static_assert(DP == 16 || DP == 32 || DP == 64 || DP == 128 || DP == 256, "DP");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN");
   static_assert(G >= 1 && G <= 8, "tiles per group");
-  static_assert(STAGES >= 1 && STAGES <= 16, "stages (one producer lane each)");
+  static_assert(STAGES >= 1 && STAGES <= 16, "stages");
   static constexpr int TM = 128;                          // rows per tile (MMA M)
   static constexpr int XW = DP * 4 <= 128 ? DP * 4 : 128; // K-major row width in bytes
   static constexpr int KSUB = DP * 4 / XW;                // 128 B sub-tiles along K
@@ -88,6 +88,11 @@ struct ProductCfg {
   static constexpr int C_BYTES = REDUCE ? 0 : DP * BN * 4;
   static constexpr int NPREC = X3 ? 2 : 1;
   static constexpr int STAGE_BYTES = NPREC * (F_BYTES + C_BYTES);   // bytes the TMA fills
+  // TMA copies per stage: per precision half, KSUB sub-tiles of F and BN / 32 of C^T; lanes
+  // 0..NLOADS-1 of the producer warp issue one each
+  static constexpr int LOADS_PER_PREC = KSUB + (REDUCE ? 0 : BN / 32);
+  static constexpr int NLOADS = NPREC * LOADS_PER_PREC;
+  static_assert(NLOADS <= 16, "one producer lane per copy");
   static constexpr bool H16 = !X3 && !REDUCE;                     // fp16 second MMA
   static constexpr int C16_BYTES = H16 ? DP * BN * 2 : 0;         // fp16 copy of the C chunk
   static constexpr int STAGE_ALLOC = STAGE_BYTES + C16_BYTES;
@@ -147,6 +152,14 @@ __device__ __forceinline__ WorkItem work_item(const ProductParams& p, int item) 
   w.c0 = split * p.chunks_per_split;
   w.c1 = min(p.n_chunks, w.c0 + p.chunks_per_split);
   return w;
+}
+
+// The ci-th chunk of an item in this CTA's order: the chunk range rotated by the CTA index, so
+// that at any moment the SMs read different chunks (the same chunk from every SM at once
+// concentrates all loads on a few L2 slices). Every role walks the same order.
+__device__ __forceinline__ int chunk_at(const WorkItem& w, int ci) {
+  const int nc = w.c1 - w.c0;
+  return w.c0 + (int)((ci + blockIdx.x) % (unsigned)nc);
 }
 
 // fp16x2 of (ReLU(lo), ReLU(hi)), round to nearest; lo in the low half.
@@ -230,61 +243,68 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
-    const bool stage_lane = lane < STAGES;
+    // lanes 0..15 fill the stages together: lane 0 waits for the stage to be free and posts the
+    // expected bytes, lane j < NLOADS issues copy j of the chunk (copies issued by one thread
+    // complete one after another, copies from different lanes overlap); lane 16 + g loads X slot g
     const int xslot = lane - 16;
     const bool x_lane = xslot >= 0 && xslot < G;
-    uint32_t fills = 0;   // loads this lane issued into its stage
-    uint32_t xuses = 0;   // loads this lane issued into its X slot
-    bool ok = true;
-    uint32_t gch = 0;     // global chunk counter, identical in every lane
-    if (stage_lane || x_lane) {
+    if (lane < 16) {
+      bool ok = true;
+      uint32_t gch = 0;     // chunks issued
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
         const WorkItem w = work_item(p, item);
-        if (x_lane) {
-          if (xslot >= w.ntiles) continue;
-          if (xuses > 0 && !mbar_wait(&x_empty[xslot], (xuses - 1) & 1, abort_flag, p.err,
-                                      DEV_TIMEOUT_X, p.timeout_ns)) { ok = false; break; }
-          uint8_t* xdst = sX + xslot * Cfg::XBUF_BYTES;
-          mbar_arrive_expect_tx(&x_full[xslot], Cfg::X_BYTES);
-#pragma unroll
-          for (int s = 0; s < Cfg::KSUB; ++s)
-            tma_load_2d(xdst + s * Cfg::TM * Cfg::XW, &tmX, s * Cfg::BOX_K,
-                        (w.tile0 + xslot) * Cfg::TM, &x_full[xslot]);
-          ++xuses;
-          continue;
-        }
-        for (int c = w.c0; c < w.c1; ++c, ++gch) {
+        for (int ci = 0; ci < w.c1 - w.c0; ++ci, ++gch) {
+          const int c = chunk_at(w, ci);
           const int stage = gch % STAGES;
-          if (stage != lane) continue;
           const uint32_t round = gch / STAGES;
-          // a stage is free once the empty barrier completed its previous round
-          if (round > 0 && !mbar_wait(&empty[stage], (round - 1) & 1, abort_flag, p.err,
-                                      DEV_TIMEOUT_EMPTY, p.timeout_ns)) { ok = false; break; }
-          uint8_t* st = sStage + stage * Cfg::STAGE_ALLOC;
-          mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-#pragma unroll
-          for (int h = 0; h < Cfg::NPREC; ++h) {
-            const CUtensorMap* tf = h == 0 ? &tmFhi : &tmFlo;
-            uint8_t* fdst = st + h * Cfg::F_BYTES;
-#pragma unroll
-            for (int s = 0; s < Cfg::KSUB; ++s)
-              tma_load_2d(fdst + s * BN * Cfg::XW, tf, s * Cfg::BOX_K, c * BN, &full[stage]);
-            if (!REDUCE) {
-              const CUtensorMap* tc = h == 0 ? &tmChi : &tmClo;
-              uint8_t* cdst = st + Cfg::NPREC * Cfg::F_BYTES + h * Cfg::C_BYTES;
-#pragma unroll
-              for (int s = 0; s < BN / 32; ++s)
-                tma_load_2d(cdst + s * DP * 128, tc, c * BN + s * 32, 0, &full[stage]);
+          int go = 1;
+          if (lane == 0) {
+            // a stage is free once the empty barrier completed its previous round
+            if (round > 0 && !mbar_wait(&empty[stage], (round - 1) & 1, abort_flag, p.err,
+                                        DEV_TIMEOUT_EMPTY, p.timeout_ns)) go = 0;
+            else mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
+          }
+          go = __shfl_sync(0xffffu, go, 0);
+          if (!go) { ok = false; break; }
+          if (lane < Cfg::NLOADS) {
+            uint8_t* st = sStage + stage * Cfg::STAGE_ALLOC;
+            const int h = lane / Cfg::LOADS_PER_PREC, r = lane % Cfg::LOADS_PER_PREC;
+            if (r < Cfg::KSUB) {
+              tma_load_2d(st + h * Cfg::F_BYTES + r * BN * Cfg::XW, h == 0 ? &tmFhi : &tmFlo,
+                          r * Cfg::BOX_K, c * BN, &full[stage]);
+            } else {
+              const int sc = r - Cfg::KSUB;
+              tma_load_2d(st + Cfg::NPREC * Cfg::F_BYTES + h * Cfg::C_BYTES + sc * DP * 128,
+                          h == 0 ? &tmChi : &tmClo, c * BN + sc * 32, 0, &full[stage]);
             }
           }
-          ++fills;
         }
       }
-      if (*abort_flag) {
-        // wait (bounded) for this lane's own copies still in flight before leaving
-        if (stage_lane && fills > 0) mbar_drain(&full[lane], (fills - 1) & 1);
-        if (x_lane && xuses > 0) mbar_drain(&x_full[xslot], (xuses - 1) & 1);
+      if (*abort_flag && lane == 0) {
+        // wait (bounded) for the copies still in flight: the last fill of every stage
+        for (uint32_t u = 1; u <= (uint32_t)STAGES && u <= gch; ++u) {
+          const uint32_t g = gch - u;
+          mbar_drain(&full[g % STAGES], (g / STAGES) & 1);
+        }
       }
+    } else if (x_lane) {
+      bool ok = true;
+      uint32_t xuses = 0;   // loads this lane issued into its X slot
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+        const WorkItem w = work_item(p, item);
+        if (xslot >= w.ntiles) continue;
+        if (xuses > 0 && !mbar_wait(&x_empty[xslot], (xuses - 1) & 1, abort_flag, p.err,
+                                    DEV_TIMEOUT_X, p.timeout_ns)) { ok = false; break; }
+        uint8_t* xdst = sX + xslot * Cfg::XBUF_BYTES;
+        mbar_arrive_expect_tx(&x_full[xslot], Cfg::X_BYTES);
+#pragma unroll
+        for (int s = 0; s < Cfg::KSUB; ++s)
+          tma_load_2d(xdst + s * Cfg::TM * Cfg::XW, &tmX, s * Cfg::BOX_K,
+                      (w.tile0 + xslot) * Cfg::TM, &x_full[xslot]);
+        ++xuses;
+      }
+      // wait (bounded) for this lane's own copies still in flight before leaving
+      if (*abort_flag && xuses > 0) mbar_drain(&x_full[xslot], (xuses - 1) & 1);
     }
   } else if (warp == 1 || warp == Cfg::MMA1B_WARP) {
     // ------------------------------------------------------------------ first MMA (S = X F^T)
@@ -305,7 +325,8 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
         for (int gi = 0; gi < w.ntiles && ok; ++gi)
           if (!mbar_wait(X3 ? &x_ready[gi] : &x_full[gi], (slot_par >> gi) & 1u, abort_flag,
                          p.err, DEV_TIMEOUT_X, p.timeout_ns)) ok = false;
-        for (int c = w.c0; c < w.c1 && ok; ++c, ++chunk) {
+        for (int ci = 0; ci < w.c1 - w.c0 && ok; ++ci, ++chunk) {
+          const int c = chunk_at(w, ci);
           const int stage = chunk % STAGES;
           if (!mbar_wait(&full[stage], (chunk / STAGES) & 1, abort_flag, p.err, DEV_TIMEOUT_FULL,
                          p.timeout_ns)) { ok = false; break; }
@@ -369,7 +390,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
       bool ok = true;
       for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
         const WorkItem w = work_item(p, item);
-        for (int c = w.c0; c < w.c1 && ok; ++c, ++chunk) {
+        for (int ci = 0; ci < w.c1 - w.c0 && ok; ++ci, ++chunk) {
           const int stage = chunk % STAGES;
           const uint32_t stg = sSt_addr + stage * Cfg::STAGE_ALLOC;
           // every issuer waits for the chunk, even one that owns no tile of this group: its
@@ -379,7 +400,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           for (int gi = 0; gi < w.ntiles; ++gi, ++pair) {
             if (gi % Cfg::N2 != me) continue;
             const uint32_t buf = pair % NBUF;
-            const bool first = c == w.c0;
+            const bool first = ci == 0;
             if (!mbar_wait(&r_ready[buf], (pair / NBUF) & 1, abort_flag, p.err, DEV_TIMEOUT_RREADY,
                            p.timeout_ns)) { ok = false; break; }
             if (first && ((slot_used >> gi) & 1u) &&
@@ -419,7 +440,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
               }
             }
             mma_commit(&s_free[buf]);
-            if (c == w.c1 - 1) mma_commit(&y_full[gi]);
+            if (ci == w.c1 - w.c0 - 1) mma_commit(&y_full[gi]);
           }
           // every first MMA of this chunk completed before the epilogue released its S, so the
           // N2 issuers' commits together cover the last readers of the stage
@@ -591,6 +612,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
       }
     }
   } else if (Cfg::H16 && warp == 2 + Cfg::EPI_WARPS) {
+    if constexpr (Cfg::H16) {
     // ------------------------------------------------------------------ C converter (warp 10)
     // fp32 C chunk (32-float SW128 sub-tiles) -> fp16, scaled by 2^ec (64-element SW128 sub-tiles)
     const float cmax = __uint_as_float(p.stats[1]);
@@ -611,25 +633,45 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
         const uint8_t* src = sStage + stage * Cfg::STAGE_ALLOC + Cfg::F_BYTES;
         uint8_t* dst = sStage + stage * Cfg::STAGE_ALLOC + Cfg::STAGE_BYTES;
         constexpr int UNITS = (BN / 64) * DP * 8;  // 16-byte fp16 units
-        for (int uidx = lane; uidx < UNITS; uidx += 32) {
-          const int u = uidx & 7;
-          const int r = (uidx >> 3) % DP;
-          const int s16 = (uidx >> 3) / DP;
-          const int k0 = 64 * s16 + 8 * u;
-          const int s32 = k0 >> 5, v0 = (k0 & 31) >> 2;
-          const uint8_t* rowp = src + s32 * (DP * 128) + r * 128;
-          const float4 a = *reinterpret_cast<const float4*>(rowp + ((v0 ^ (r & 7)) << 4));
-          const float4 b = *reinterpret_cast<const float4*>(rowp + (((v0 + 1) ^ (r & 7)) << 4));
-          __half2 h[4] = {__floats2half2_rn(a.x * cscale, a.y * cscale),
-                          __floats2half2_rn(a.z * cscale, a.w * cscale),
-                          __floats2half2_rn(b.x * cscale, b.y * cscale),
-                          __floats2half2_rn(b.z * cscale, b.w * cscale)};
-          *reinterpret_cast<uint4*>(dst + s16 * (DP * 128) + r * 128 + ((u ^ (r & 7)) << 4)) =
-              *reinterpret_cast<const uint4*>(h);
+        static_assert(UNITS % 32 == 0, "whole rounds of the converter warp");
+        // batches of UB units per lane: all loads of a batch are issued before its stores, so
+        // they are in flight together (source and destination share the shared-memory array,
+        // so the compiler would not hoist loads above earlier stores by itself); at Dp = 64
+        // with 2-tile groups the converter otherwise paces the kernel
+        constexpr int PER_LANE = UNITS / 32;
+        constexpr int UB = PER_LANE < 8 ? PER_LANE : 8;
+        static_assert(PER_LANE % UB == 0, "converter batches");
+        for (int b0 = 0; b0 < PER_LANE; b0 += UB) {
+          float4 va[UB], vb[UB];
+#pragma unroll
+          for (int q = 0; q < UB; ++q) {
+            const int uidx = lane + 32 * (b0 + q);
+            const int u = uidx & 7;
+            const int r = (uidx >> 3) % DP;
+            const int k0 = 64 * ((uidx >> 3) / DP) + 8 * u;
+            const int s32 = k0 >> 5, v0 = (k0 & 31) >> 2;
+            const uint8_t* rowp = src + s32 * (DP * 128) + r * 128;
+            va[q] = *reinterpret_cast<const float4*>(rowp + ((v0 ^ (r & 7)) << 4));
+            vb[q] = *reinterpret_cast<const float4*>(rowp + (((v0 + 1) ^ (r & 7)) << 4));
+          }
+#pragma unroll
+          for (int q = 0; q < UB; ++q) {
+            const int uidx = lane + 32 * (b0 + q);
+            const int u = uidx & 7;
+            const int r = (uidx >> 3) % DP;
+            const int s16 = (uidx >> 3) / DP;
+            __half2 h[4] = {__floats2half2_rn(va[q].x * cscale, va[q].y * cscale),
+                            __floats2half2_rn(va[q].z * cscale, va[q].w * cscale),
+                            __floats2half2_rn(vb[q].x * cscale, vb[q].y * cscale),
+                            __floats2half2_rn(vb[q].z * cscale, vb[q].w * cscale)};
+            *reinterpret_cast<uint4*>(dst + s16 * (DP * 128) + r * 128 + ((u ^ (r & 7)) << 4)) =
+                *reinterpret_cast<const uint4*>(h);
+          }
         }
         fence_proxy_async_smem();
         mbar_arrive(&c16_ready[stage]);
       }
+    }
     }
   } else if (X3 && warp == 2 + Cfg::EPI_WARPS) {
     // ------------------------------------------------------------------ X splitter (warp 10)
