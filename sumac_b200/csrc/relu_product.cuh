@@ -19,8 +19,8 @@
 //   warp 0       TMA producer: lanes 0..15 fill each stage (F chunk, C^T chunk) together, one
 //                copy per lane; lane 16 + g owns X slot g. Copies issued by one thread complete
 //                one after another, copies from different lanes overlap.
-//   warp 1, last first-MMA issuers (one thread each, even / odd pairs): S = X_g F_c^T into the
-//                next of NBUF TMEM buffers (kind::tf32)
+//   warp 1       first-MMA issuer (one thread): S = X_g F_c^T into the next of NBUF TMEM
+//                buffers (kind::tf32); in TF32 reduce mode warp 10 issues the odd pairs
 //   warps 2..9   epilogue, two warps per TMEM lane quadrant, each on half of the columns:
 //                tcgen05.ld S -> ReLU -> tcgen05.st R (or accumulate the sums); at the end of a
 //                group tcgen05.ld of each Y_g -> global
@@ -30,12 +30,12 @@
 //                group): Y_g += R C_c with R read from TMEM once the epilogue has rewritten
 //                that S as R = ReLU(S); the commit hands the S buffer back to warp 1.
 //
-// Cost model (measured on B200): at small rank the kernel is bound by the serial latency of
-// issuing tcgen05 instructions (~50 ns per MMA or commit from one thread, whatever N <= 64;
-// the second MMA has N = Dp and needs BN / 16 fp16 or BN / 8 tf32 instructions per pair) and by
-// the epilogue's TMEM round trip, not by tensor throughput. Three issuing threads and the
-// resident tile groups (a chunk copy from L2 takes 1.5-3 us to land when every SM reads the
-// same lines) keep those off each other's critical path.
+// Cost model (measured on B200 with in-kernel timestamps): at small rank the kernel is bound by
+// serial latencies, not by tensor throughput or HBM: ~50 ns per tcgen05 MMA or commit issued by
+// one thread (whatever N <= 64; the second MMA has N = Dp and needs BN / 16 fp16 or BN / 8 tf32
+// instructions per pair), the epilogue's TMEM round trip (~350 ns per pair), and at Dp = 64 with
+// 2-tile groups the per-chunk fp16 conversion of C. Resident tile groups (a chunk copy from L2
+// takes 1.5-4 us to land), two second-MMA issuers and batched conversion keep these apart.
 //
 // Precision: X3=false is TF32 for S = X F^T (the tensor core reads the fp32 bits as tf32), and
 // the second MMA runs in fp16 (same 10-bit mantissa) with R and C scaled by exact powers of two
