@@ -66,6 +66,12 @@ size_t sumac_noalloc_scratch_bytes(void) { return SCRATCH_BYTES; }
 int sumac_relu_bat_reduce_noalloc(const float* A, const float* B, int64_t M, int64_t N, int D,
                                   double* out, int precision, int* dev_err,
                                   sumac_stream_t stream) {
+  // shape and pointer checks come first, so that a bad argument is reported as such (a negative
+  // M or N would otherwise wrap to a huge scratch size and read as "too large")
+  if (M <= 0 || N <= 0 || D <= 0)
+    return sb::set_last_error(SUMAC_ERR_ARG, "relu_bat_reduce_noalloc: empty or negative shape");
+  if (!A || !B || !out || !dev_err)
+    return sb::set_last_error(SUMAC_ERR_ARG, "relu_bat_reduce_noalloc: null pointer");
   const size_t need = sumac_relu_bat_reduce_workspace_bytes(M, N, D, precision);
   if (need > SCRATCH_BYTES) {
     char msg[256];

@@ -54,6 +54,20 @@
 
 namespace sb {
 
+// Optional in-kernel timeline (build with -DSB_TRACE): CTA 0 stamps clock64() at each hand-off of
+// the pipeline into g_sb_trace[event][index]; sumac_debug_trace copies it out. Off by default.
+#ifdef SB_TRACE
+__device__ unsigned long long g_sb_trace[16][512];
+#define SB_TR(ev, i)                                                         \
+  do {                                                                       \
+    if (blockIdx.x == 0 && (unsigned)(i) < 512u) g_sb_trace[ev][i] = clock64(); \
+  } while (0)
+#else
+#define SB_TR(ev, i) \
+  do {               \
+  } while (0)
+#endif
+
 struct ProductParams {
   int M;                 // rows of X
   int N;                 // rows of F (columns of C^T)
@@ -126,10 +140,19 @@ struct ProductCfg {
   static constexpr int N2 = 2;
   // first-MMA issuers: in TF32 reduce mode warp 1 takes the even pairs and warp MMA1B_WARP the
   // odd ones (measured 15% faster at the reference's reduce shapes); elsewhere warp 1 alone (a
-  // second issuer gave no gain in product mode, and in 3xTF32 product mode at C4's shapes it
-  // ran into a bounded-wait timeout whose cause is not understood, so it is not used there)
+  // second issuer gave no gain in product mode, and there its s_free waits can meet commits that
+  // arrive out of order; see the phase-lag assertion below)
   static constexpr int N1 = (REDUCE && !X3) ? 2 : 1;
   static constexpr int MMA1B_WARP = N1 == 2 ? 10 : 1;
+  // mbarrier parity waits are only sound when the waiter is at most one phase ahead of the
+  // barrier. A second-MMA issuer owns the tiles gi % N2 == me, so two of its consecutive pairs
+  // can lie up to 2 N2 - 1 pairs apart (one owned tile in a group of 2 N2 - 1 tiles); its wait on
+  // r_ready of the later pair then needs the epilogue to have released the pair NBUF earlier,
+  // i.e. NBUF >= 2 N2 - 1. With N1 > 1 first-MMA issuers in product mode, the s_free commits of
+  // different second-MMA issuers can reach a buffer's barrier out of order, so product mode keeps
+  // one first-MMA issuer. In reduce mode the epilogue releases the buffers in pair order and an
+  // issuer's pairs are N1 apart, so N1 <= NBUF suffices.
+  static_assert(REDUCE ? N1 <= NBUF : (N1 == 1 && NBUF >= 2 * N2 - 1), "barrier phase lag");
   static constexpr int THREADS =
       REDUCE ? 32 * (N1 == 2 ? 11 : 10 + (AUX ? 1 : 0)) : 32 * (MMA2_WARP + N2);
   // mbarriers, TMEM slot and abort flag sit below the epilogue's reduction scratch at +768 B
@@ -240,6 +263,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_slot;
+  if (threadIdx.x == 0) SB_TR(15, 0);
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -266,6 +290,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           }
           go = __shfl_sync(0xffffu, go, 0);
           if (!go) { ok = false; break; }
+          if (lane == 0) SB_TR(0, gch);
           if (lane < Cfg::NLOADS) {
             uint8_t* st = sStage + stage * Cfg::STAGE_ALLOC;
             const int h = lane / Cfg::LOADS_PER_PREC, r = lane % Cfg::LOADS_PER_PREC;
@@ -302,6 +327,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           tma_load_2d(xdst + s * Cfg::TM * Cfg::XW, &tmX, s * Cfg::BOX_K,
                       (w.tile0 + xslot) * Cfg::TM, &x_full[xslot]);
         ++xuses;
+        SB_TR(14, xslot);
       }
       // wait (bounded) for this lane's own copies still in flight before leaving
       if (*abort_flag && xuses > 0) mbar_drain(&x_full[xslot], (xuses - 1) & 1);
@@ -343,6 +369,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
               break;
             }
             tc_fence_after();
+            SB_TR(1, pair);
             const uint32_t xaddr = sX_addr + gi * Cfg::XBUF_BYTES;
             const uint32_t s_tm = tbase + buf * BN;
 #pragma unroll
@@ -366,6 +393,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
               }
             }
             mma_commit(&s_full[buf]);
+            SB_TR(2, pair);
           }
           // reduce mode: the first MMAs are the stage's only readers
           if (REDUCE && ok) mma_commit(&empty[stage]);
@@ -407,6 +435,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
                 !mbar_wait(&y_empty[gi], ((slot_par >> gi) & 1u) ^ 1u, abort_flag, p.err,
                            DEV_TIMEOUT_Y, p.timeout_ns)) { ok = false; break; }
             tc_fence_after();
+            SB_TR(7 + 2 * me, pair);
             const uint32_t s_hi = tbase + buf * BN;
             const uint32_t ytm = tbase + Cfg::TMEM_Y + gi * DP;
             if constexpr (Cfg::H16) {
@@ -440,6 +469,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
               }
             }
             mma_commit(&s_free[buf]);
+            SB_TR(8 + 2 * me, pair);
             if (ci == w.c1 - w.c0 - 1) mma_commit(&y_full[gi]);
           }
           // every first MMA of this chunk completed before the epilogue released its S, so the
@@ -505,6 +535,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           if (!mbar_wait(&s_full[buf], (pair / NBUF) & 1, abort_flag, p.err, DEV_TIMEOUT_SFULL,
                          p.timeout_ns)) { ok = false; break; }
           tc_fence_after();
+          if (warp == 2 && lane == 0) SB_TR(3, pair);
           const uint32_t s_tm = tbase + lane_addr + buf * BN + half * Cfg::EPI_COLS;
           float v[Cfg::EPI_COLS];
           if constexpr (Cfg::LDW == 32) {
@@ -561,6 +592,8 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           }
           tc_fence_before();
           mbar_arrive(&r_ready[buf]);
+          if (lane == 0 && warp == 2) SB_TR(5, pair);
+          if (lane == 0 && warp == 9) SB_TR(6, pair);
         }
       }
       if (!ok) break;
@@ -570,6 +603,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           if (!mbar_wait(&y_full[gi], (slot_par >> gi) & 1u, abort_flag, p.err, DEV_TIMEOUT_Y,
                          p.timeout_ns)) { ok = false; break; }
           tc_fence_after();
+          if (warp == 2 && lane == 0) SB_TR(12, gi);
           const int row = (w.tile0 + gi) * Cfg::TM + row_in_tile;
           const float inv = Cfg::H16 ? __int_as_float((127 - er[gi] - ec) << 23) : 1.f;
           float* out = p.ws + ((size_t)split * p.M + (size_t)(row < p.M ? row : 0)) * DP;
@@ -589,6 +623,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           }
           tc_fence_before();
           mbar_arrive(&y_empty[gi]);
+          if (warp == 2 && lane == 0) SB_TR(13, gi);
         }
       }
       slot_par ^= (1u << w.ntiles) - 1u;
@@ -670,6 +705,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
         }
         fence_proxy_async_smem();
         mbar_arrive(&c16_ready[stage]);
+        if (lane == 0) SB_TR(11, gch);
       }
     }
     }
@@ -700,6 +736,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
   __syncwarp();
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) SB_TR(15, 1);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, 512);

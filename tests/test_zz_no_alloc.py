@@ -75,3 +75,15 @@ def test_noalloc_rejects_problem_larger_than_scratch():
                                            torch.cuda.current_stream().cuda_stream)
     assert rc == -3
     assert b"fixed scratch" in lib.sumac_last_error()
+
+
+@pytest.mark.parametrize("M,N,D", [(-5, 8, 16), (100, -1, 16), (100, 8, 0)])
+def test_noalloc_rejects_bad_shapes_as_argument_errors(M, N, D):
+    lib = _native.lib()
+    A = torch.empty((8, 16), device="cuda")
+    out = torch.zeros(2, dtype=torch.float64, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    rc = lib.sumac_relu_bat_reduce_noalloc(A.data_ptr(), A.data_ptr(), M, N, D, out.data_ptr(),
+                                           _native.SUMAC_3XTF32, err.data_ptr(),
+                                           torch.cuda.current_stream().cuda_stream)
+    assert rc == -1  # SUMAC_ERR_ARG, not the scratch-size error
