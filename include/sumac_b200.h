@@ -72,6 +72,18 @@ int sumac_relu_bat_c(const float* A, const float* B, const float* C, int64_t M, 
                      sumac_stream_t stream);
 
 /*
+ * relu_bat_c with a choice of the elementwise map applied to S = B A^T before the contraction:
+ * SUMAC_RELU gives relu_bat_c; SUMAC_STEP gives Y = step(B A^T) C with step(s) = 1 for s > 0 and
+ * 0 otherwise, the mask product in the gradient of sum ReLU(A B^T) that the reference forms densely
+ * in src/sumac/kernels/relu_bat_reduce_jit/custom_op.py:74-82 (relu_mask @ B, relu_mask.T @ A).
+ * Same workspace as sumac_relu_bat_c.
+ */
+enum { SUMAC_RELU = 0, SUMAC_STEP = 1 };
+int sumac_relu_bat_c_mode(const float* A, const float* B, const float* C, int64_t M, int64_t N,
+                          int D, float* Y, int precision, int mode, void* ws, size_t ws_bytes,
+                          int* dev_err, sumac_stream_t stream);
+
+/*
  * relu_bat_reduce: out[0] = sum ReLU(A B^T), out[1] = sum ReLU(A B^T)^2 (double, device), with
  * A[M][D], B[N][D] unpadded. Replaces sumac::relu_bat_reduce_fused
  * (src/sumac/kernels/relu_bat_reduce_jit/custom_op.py:7-18 -> jit_kernel.py:87-132).

@@ -39,6 +39,7 @@ _SIGS = {
     "sumac_relu_product": (i32, [p, i64, p, p, p, p, i64, i64, i32, i32, p, p, p]),
     "sumac_relu_bat_c_workspace_bytes": (sz, [i64, i64, i32, i32]),
     "sumac_relu_bat_c": (i32, [p, p, p, i64, i64, i32, p, i32, p, sz, p, p]),
+    "sumac_relu_bat_c_mode": (i32, [p, p, p, i64, i64, i32, p, i32, i32, p, sz, p, p]),
     "sumac_relu_bat_reduce_workspace_bytes": (sz, [i64, i64, i32, i32]),
     "sumac_relu_bat_reduce": (i32, [p, p, i64, i64, i32, p, i32, p, sz, p, p]),
     "sumac_noalloc_scratch_bytes": (sz, []),

@@ -50,8 +50,10 @@ class SumacConfig:
     """Same fields and defaults as sumac's SumacConfig (options.py:45-157).
 
     Additional opt-in fields (defaults keep the reference's behaviour):
-      perm_device: device of the generators that draw the row permutations (default: the training
-        device, as the reference). "cpu" reproduces the permutations of a CPU run of the reference.
+      perm_device: device of the random generators, the ones that draw the row permutations and
+        the one that draws the initial factors (default: the training device, as the reference).
+        "cpu" reproduces the random draws of a CPU run of the reference; the arithmetic still runs
+        on the training device.
       tf32_mode: None (follow allow_tf32: TF32 if True, 3xTF32 fp32-accurate otherwise), or one of
         "tf32", "3xtf32".
     """
@@ -169,9 +171,9 @@ class SumacConfig:
     def get_generator(self):
         """(gen, gen_rows, gen_aux) seeded seed, seed+1, seed+2 (options.py:282-296). The first
         two live on the training device; the third on it for SALSA and on the CPU for GD.
-        With perm_device set, the permutation generators live there instead."""
+        With perm_device set, the generators live there instead."""
         dev = self.perm_device if self.perm_device is not None else self.device
-        gen = torch.Generator(device=self.device)
+        gen = torch.Generator(device=dev)
         gen_rows = torch.Generator(device=dev)
         tmp_device = dev if self.method == SumacMethod.SALSA else "cpu"
         gen_aux = torch.Generator(device=tmp_device)

@@ -161,7 +161,16 @@ size_t sumac_relu_bat_c_workspace_bytes(int64_t M, int64_t N, int D, int precisi
 int sumac_relu_bat_c(const float* A, const float* B, const float* C, int64_t M, int64_t N, int D,
                      float* Y, int precision, void* ws, size_t ws_bytes, int* dev_err,
                      sumac_stream_t stream) {
+  return sumac_relu_bat_c_mode(A, B, C, M, N, D, Y, precision, SUMAC_RELU, ws, ws_bytes, dev_err,
+                               stream);
+}
+
+int sumac_relu_bat_c_mode(const float* A, const float* B, const float* C, int64_t M, int64_t N,
+                          int D, float* Y, int precision, int mode, void* ws, size_t ws_bytes,
+                          int* dev_err, sumac_stream_t stream) {
   const bool x3 = precision == SUMAC_3XTF32;
+  if (mode != SUMAC_RELU && mode != SUMAC_STEP)
+    return fail(SUMAC_ERR_ARG, "relu_bat_c: mode %d is neither SUMAC_RELU nor SUMAC_STEP", mode);
   const int Dp = padded(D);
   if (M <= 0 || N <= 0 || D <= 0) return fail(SUMAC_ERR_ARG, "relu_bat_c: empty shape M=%lld N=%lld D=%d", (long long)M, (long long)N, D);
   if (!A || !B || !C || !Y || !dev_err) return fail(SUMAC_ERR_ARG, "relu_bat_c: null pointer");
@@ -178,7 +187,7 @@ int sumac_relu_bat_c(const float* A, const float* B, const float* C, int64_t M, 
   launch_transpose_split(p.Cp, N, Dp, p.Cthi, p.Ctlo, p.ldct, s);
   if (!x3) launch_operand_stats(p.Fp, N, Dp, p.Cthi, (int64_t)Dp * p.ldct, p.stats, s);
   int rc = launch_relu_product(p.Xp, M, p.Fp, p.Flo, p.Cthi, p.Ctlo, p.ldct, N, Dp, x3, p.part,
-                               dev_err, sms, g_timeout_ns, s, p.stats);
+                               dev_err, sms, g_timeout_ns, s, p.stats, mode == SUMAC_STEP);
   if (rc) return cuda_status(rc, "relu_bat_c");
   FinalizeArgs f{};
   f.mode = FIN_STORE; f.M = M; f.Dp = Dp; f.splits = product_split_count(M, N, Dp, x3, sms);
@@ -341,7 +350,7 @@ int sumac_salsa_block_update(const float* F, int64_t m_fixed, const int64_t* row
   if (b <= 0 || M <= 0 || m_fixed <= 0) return fail(SUMAC_ERR_ARG, "salsa_block_update: empty shape");
   if (!F || !rows || !X || !dX || !unbias || !dev_err || (rowptr && !ent))
     return fail(SUMAC_ERR_ARG, "salsa_block_update: null pointer");
-  if (!Dp || d > 128 || !product_supported(Dp, x3))
+  if (!Dp || !product_supported(Dp, x3))
     return fail(SUMAC_ERR_UNSUPPORTED, "salsa_block_update: rank %d not supported with precision %d", d, precision);
   if (!aligned16(F) || !aligned16(X) || !aligned16(dX))
     return fail(SUMAC_ERR_ARG, "salsa_block_update: factors must be 16-byte aligned");

@@ -39,7 +39,7 @@ __global__ void gather_pad_kernel(const float* __restrict__ src, int64_t ld_src,
     if (dhi) {
       const float h = tf32_hi(x);
       dhi[i] = h;
-      if (dlo) dlo[i] = x - h;
+      if (dlo) dlo[i] = tf32_lo(x, h);
     }
   }
 }
@@ -75,7 +75,7 @@ __global__ void transpose_split_kernel(const float* __restrict__ src, int64_t nr
       if (dlo) {
         const float h = tf32_hi(x);
         dhi[c * ld_dst + r] = h;
-        dlo[c * ld_dst + r] = x - h;
+        dlo[c * ld_dst + r] = tf32_lo(x, h);
       } else {
         dhi[c * ld_dst + r] = x;
       }
@@ -204,7 +204,7 @@ __global__ void solve_kernel(const float* __restrict__ FI, int64_t b, int d, int
   }
   const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= b) return;
-  double x[128];
+  double x[256];
   for (int c = 0; c < d; ++c) x[c] = (double)FI[r * Dp + c];
   for (int k = 0; k < d; ++k) {
     const int p = piv[k];
@@ -226,7 +226,7 @@ __global__ void solve_kernel(const float* __restrict__ FI, int64_t b, int d, int
     if (Ctlo) {
       const float h = tf32_hi(v);
       Cthi[c * ldct + r] = h;
-      Ctlo[c * ldct + r] = v - h;
+      Ctlo[c * ldct + r] = tf32_lo(v, h);
     } else {
       Cthi[c * ldct + r] = v;
     }
@@ -333,7 +333,7 @@ __global__ void salsa_gram_kernel(const float* __restrict__ Ffix, const int64_t*
     if (Fhi) {
       const float h = tf32_hi(v);
       Fhi[o] = h;
-      Flo[o] = v - h;
+      Flo[o] = tf32_lo(v, h);
     }
   }
   __syncthreads();
@@ -416,7 +416,7 @@ __global__ void __launch_bounds__(128) salsa_solve_kernel(const float* __restric
     if (Ctlo) {
       const float h = tf32_hi(v);
       Cthi[c * ldct + r] = h;
-      Ctlo[c * ldct + r] = v - h;
+      Ctlo[c * ldct + r] = tf32_lo(v, h);
     } else {
       Cthi[c * ldct + r] = v;
     }
@@ -752,7 +752,7 @@ static constexpr int CSR_LONG_GAP = 64;
 struct CsrLayout {
   int ncta;
   int64_t chunk;
-  size_t off_perm_inv, off_hist, off_keys, off_ntask, off_tasks, total;
+  size_t off_perm_inv, off_hist, off_totals, off_keys, off_ntask, off_tasks, total;
   int64_t max_tasks;
 };
 
@@ -768,6 +768,7 @@ static CsrLayout csr_layout(int64_t m_fixed, int64_t nnz, int num_blocks, int64_
   size_t o = 0;
   L.off_perm_inv = o; o = al(o + sizeof(int32_t) * (size_t)(m_fixed > 0 ? m_fixed : 1));
   L.off_hist = o; o = al(o + sizeof(int32_t) * (size_t)num_blocks * L.ncta);
+  L.off_totals = o; o = al(o + sizeof(int32_t) * (size_t)num_blocks);
   L.off_keys = o; o = al(o + sizeof(int32_t) * (size_t)(nnz > 0 ? nnz : 1));
   L.off_ntask = o; o = al(o + 16);
   L.max_tasks = ((int64_t)num_blocks * M) / CSR_LONG_GAP + 4;
@@ -796,25 +797,35 @@ __global__ void csr_hist_kernel(const int32_t* __restrict__ e_fixed, int64_t nnz
   __syncthreads();
   const int64_t e0 = (int64_t)blockIdx.x * chunk;
   const int64_t e1 = min(nnz, e0 + chunk);
-  for (int64_t e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
-    const int blk = inv[e_fixed[e]] / bs;
-    atomicAdd(&sh[blk], 1);
+  constexpr int IT = 4;  // edges per thread in flight
+  const unsigned lane_lt = (1u << (threadIdx.x & 31)) - 1u;
+  for (int64_t rb = e0; rb < e1; rb += (int64_t)blockDim.x * IT) {
+    int fx[IT];
+#pragma unroll
+    for (int j = 0; j < IT; ++j) {
+      const int64_t e = rb + (int64_t)j * blockDim.x + threadIdx.x;
+      fx[j] = e < e1 ? e_fixed[e] : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < IT; ++j) {
+      const int blk = fx[j] >= 0 ? inv[fx[j]] / bs : -1;
+      // one shared-memory atomic per distinct block in the warp
+      const unsigned peers = __match_any_sync(0xffffffffu, blk);
+      if (blk >= 0 && (peers & lane_lt) == 0) atomicAdd(&sh[blk], __popc(peers));
+    }
   }
   __syncthreads();
   for (int k = threadIdx.x; k < nb; k += blockDim.x) hist[(int64_t)k * gridDim.x + blockIdx.x] = sh[k];
 }
 
-// single-CTA exclusive scan (in place) over n ints
-__global__ void scan_exclusive_kernel(int32_t* __restrict__ a, int64_t n) {
+// Exclusive scan of hist[nb][ncta] in row-major (block-major) order, in two launches: each CTA
+// of csr_scan_rows_kernel scans one row k in place (ncta <= 1024 entries, one per thread) and
+// writes its total; each CTA of csr_scan_add_kernel adds the sum of the totals of the rows before
+// its row (computed by the CTA itself, in a fixed order).
+__device__ __forceinline__ int32_t block_exclusive_scan_1024(int32_t v, int32_t* total) {
   __shared__ int32_t wsum[32];
-  const int T = blockDim.x;
-  const int64_t per = (n + T - 1) / T;
-  const int64_t s0 = threadIdx.x * per;
-  const int64_t s1 = min(n, s0 + per);
-  int32_t local = 0;
-  for (int64_t i = s0; i < s1; ++i) local += a[i];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  int32_t incl = local;
+  int32_t incl = v;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int32_t t = __shfl_up_sync(0xffffffffu, incl, o);
@@ -823,21 +834,122 @@ __global__ void scan_exclusive_kernel(int32_t* __restrict__ a, int64_t n) {
   if (lane == 31) wsum[w] = incl;
   __syncthreads();
   if (w == 0) {
-    int32_t ws = lane < (T >> 5) ? wsum[lane] : 0;
+    const int nw = (blockDim.x + 31) >> 5;
+    const int32_t ws = lane < nw ? wsum[lane] : 0;
     int32_t wi = ws;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int32_t t = __shfl_up_sync(0xffffffffu, wi, o);
       if (lane >= o) wi += t;
     }
-    if (lane < (T >> 5)) wsum[lane] = wi - ws;
+    if (lane < nw) wsum[lane] = wi - ws;
+    if (lane == 31) *total = wi;
   }
   __syncthreads();
-  int32_t run = wsum[w] + incl - local;
-  for (int64_t i = s0; i < s1; ++i) {
-    const int32_t t = a[i];
-    a[i] = run;
-    run += t;
+  return wsum[w] + incl - v;
+}
+
+__global__ void csr_scan_rows_kernel(int32_t* __restrict__ hist, int ncta,
+                                     int32_t* __restrict__ totals) {
+  __shared__ int32_t tot;
+  int32_t* row = hist + (int64_t)blockIdx.x * ncta;
+  const int32_t v = (int)threadIdx.x < ncta ? row[threadIdx.x] : 0;
+  const int32_t ex = block_exclusive_scan_1024(v, &tot);
+  if ((int)threadIdx.x < ncta) row[threadIdx.x] = ex;
+  if (threadIdx.x == 0) totals[blockIdx.x] = tot;
+}
+
+__global__ void csr_scan_add_kernel(int32_t* __restrict__ hist, int ncta,
+                                    const int32_t* __restrict__ totals) {
+  __shared__ int32_t part[32];
+  const int k = blockIdx.x;
+  int32_t s = 0;
+  for (int i = threadIdx.x; i < k; i += blockDim.x) s += totals[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = s;
+  __syncthreads();
+  int32_t base = 0;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) base += part[w];
+  int32_t* row = hist + (int64_t)k * ncta;
+  for (int i = threadIdx.x; i < ncta; i += blockDim.x) row[i] += base;
+}
+
+// Scatter with IT edges per thread per round (up to 256 * IT edges in flight per CTA). Within a
+// round the edges are ordered item-major (edge rb + j * 256 + t is item j of thread t), and a
+// block's positions follow that order: the count of each (item, warp) segment is scanned per
+// block in shared memory. Keeps the stable order of the single-item scatter below.
+template <int IT>
+__global__ void __launch_bounds__(256)
+    csr_scatter_multi_kernel(const int32_t* __restrict__ e_fixed, const int32_t* __restrict__ e_out,
+                             const float* __restrict__ e_val, int64_t nnz, int64_t chunk,
+                             const int32_t* __restrict__ inv, int bs, int nb, int64_t M,
+                             const int32_t* __restrict__ offs, int32_t* __restrict__ keys,
+                             int2* __restrict__ ent) {
+  constexpr int S = IT * 8;  // (item, warp) segments per round
+  extern __shared__ int sm[];
+  int* base = sm;             // [nb] next free position of each block
+  int* cnt = sm + nb;         // [nb][S] segment counts (zero between rounds)
+  int* pre = cnt + nb * S;    // [nb][S] segment start positions of this round
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int k = threadIdx.x; k < nb; k += blockDim.x) base[k] = offs[(int64_t)k * gridDim.x + blockIdx.x];
+  for (int k = threadIdx.x; k < nb * S; k += blockDim.x) cnt[k] = 0;
+  __syncthreads();
+  const int64_t e0 = (int64_t)blockIdx.x * chunk;
+  const int64_t e1 = min(nnz, e0 + chunk);
+  const unsigned lt_mask = (1u << lane) - 1u;
+  for (int64_t rb = e0; rb < e1; rb += 256 * IT) {
+    int blk[IT], loc[IT], rank[IT];
+#pragma unroll
+    for (int j = 0; j < IT; ++j) {
+      const int64_t e = rb + j * 256 + threadIdx.x;
+      blk[j] = e < e1 ? e_fixed[e] : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < IT; ++j) {
+      if (blk[j] >= 0) {
+        const int pos = inv[blk[j]];
+        blk[j] = pos / bs;
+        loc[j] = pos - blk[j] * bs;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < IT; ++j) {
+      const unsigned peers = __match_any_sync(0xffffffffu, blk[j]);
+      rank[j] = __popc(peers & lt_mask);
+      if (blk[j] >= 0 && rank[j] == 0) cnt[blk[j] * S + j * 8 + warp] = __popc(peers);
+    }
+    __syncthreads();
+    // per block: exclusive scan of its S segment counts on top of its running base
+    for (int b = warp; b < nb; b += 8) {
+      int v0 = lane < S ? cnt[b * S + lane] : 0;
+      int v1 = lane + 32 < S ? cnt[b * S + lane + 32] : 0;
+      int i0 = v0, i1 = v1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int t0 = __shfl_up_sync(0xffffffffu, i0, o);
+        const int t1 = __shfl_up_sync(0xffffffffu, i1, o);
+        if (lane >= o) { i0 += t0; i1 += t1; }
+      }
+      const int tot0 = __shfl_sync(0xffffffffu, i0, 31);
+      const int tot1 = __shfl_sync(0xffffffffu, i1, 31);
+      const int run = base[b];
+      if (lane < S) { pre[b * S + lane] = run + i0 - v0; cnt[b * S + lane] = 0; }
+      if (lane + 32 < S) { pre[b * S + lane + 32] = run + tot0 + i1 - v1; cnt[b * S + lane + 32] = 0; }
+      __syncwarp();
+      if (lane == 0) base[b] = run + tot0 + tot1;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < IT; ++j) {
+      if (blk[j] >= 0) {
+        const int64_t e = rb + j * 256 + threadIdx.x;
+        const int pos = pre[blk[j] * S + j * 8 + warp] + rank[j];
+        keys[pos] = (int32_t)((int64_t)blk[j] * M + e_out[e]);
+        ent[pos] = make_int2(loc[j], __float_as_int(e_val[e]));
+      }
+    }
+    __syncthreads();
   }
 }
 
@@ -930,6 +1042,7 @@ int launch_block_csr(const int64_t* perm, int64_t m_fixed, int num_blocks, const
   uint8_t* w = static_cast<uint8_t*>(ws);
   int32_t* inv = reinterpret_cast<int32_t*>(w + L.off_perm_inv);
   int32_t* hist = reinterpret_cast<int32_t*>(w + L.off_hist);
+  int32_t* totals = reinterpret_cast<int32_t*>(w + L.off_totals);
   int32_t* keys = reinterpret_cast<int32_t*>(w + L.off_keys);
   int* ntask = reinterpret_cast<int*>(w + L.off_ntask);
   int4* tasks = reinterpret_cast<int4*>(w + L.off_tasks);
@@ -941,7 +1054,18 @@ int launch_block_csr(const int64_t* perm, int64_t m_fixed, int num_blocks, const
     csr_hist_kernel<<<L.ncta, CSR_THREADS, num_blocks * sizeof(int), stream>>>(
         e_fixed, nnz, L.chunk, inv, bs, num_blocks, hist);
     count_launch();
-    scan_exclusive_kernel<<<1, 1024, 0, stream>>>(hist, (int64_t)num_blocks * L.ncta);
+    csr_scan_rows_kernel<<<num_blocks, 1024, 0, stream>>>(hist, L.ncta, totals);
+    count_launch();
+    csr_scan_add_kernel<<<num_blocks, 256, 0, stream>>>(hist, L.ncta, totals);
+    // four edges per thread per round while the block table fits comfortably in shared memory
+    const size_t smem4 = (size_t)(1 + 2 * 32) * num_blocks * sizeof(int);
+    if (smem4 <= 48 * 1024) {
+      count_launch();
+      csr_scatter_multi_kernel<4><<<L.ncta, CSR_THREADS, smem4, stream>>>(
+          e_fixed, e_out, e_val, nnz, L.chunk, inv, bs, num_blocks, M, hist, keys, ent);
+      goto scattered;
+    }
+    {
     const size_t smem = (size_t)9 * num_blocks * sizeof(int);
     static int scatter_smem_set = 0;  // largest opt-in so far (set eagerly before any capture)
     if (smem > 48 * 1024 && (int)smem > scatter_smem_set) {
@@ -951,6 +1075,8 @@ int launch_block_csr(const int64_t* perm, int64_t m_fixed, int num_blocks, const
     count_launch();
     csr_scatter_kernel<<<L.ncta, CSR_THREADS, smem, stream>>>(e_fixed, e_out, e_val, nnz, L.chunk,
                                                              inv, bs, num_blocks, M, hist, keys, ent);
+    }
+  scattered:;
   }
   const int64_t nkeys = (int64_t)num_blocks * M;
   count_launch();

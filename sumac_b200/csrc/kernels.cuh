@@ -13,12 +13,13 @@ long long launch_count();
 
 // ---- fused product / reduce (product.cu) ---------------------------------------------------
 // X [M][Dp], F{hi,lo} [N][Dp], Ct{hi,lo} [Dp][ldct] (row-major, 16-byte aligned rows).
-// Writes ws[splits][M][Dp] partial products (splits = product_split_count(...)). Returns 0 or a
+// Writes ws[splits][M][Dp] partial products (splits = product_split_count(...)); step = 1 replaces
+// ReLU(S) by the 0/1 step of S. Returns 0 or a
 // cudaError_t value; -1 for an unsupported (Dp, x3) combination, -5 bad sizes, -6 tensor map.
 int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float* Flo,
                         const float* Cthi, const float* Ctlo, int64_t ldct, int64_t N, int Dp,
                         bool x3, float* ws, int* err, int num_sms, unsigned long long timeout_ns,
-                        cudaStream_t stream, const unsigned int* stats);
+                        cudaStream_t stream, const unsigned int* stats, int step = 0);
 // stats[0] = bits of max_r |F[r]| (row norm over Dp), stats[1] = bits of max |C| over nC values
 // (atomicMax on non-negative float bits; the words must be zero beforehand). The TF32 product
 // (fp16 second MMA) reads them to pick exact power-of-two scales.

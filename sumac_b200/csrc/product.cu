@@ -44,6 +44,7 @@ static bool make_map(CUtensorMap* m, const float* base, uint64_t inner, uint64_t
 struct ProdCfgRt {
   int bn, stages, g;  // chunk rows, pipeline stages, row tiles per group
   bool ok;
+  bool simt = false;  // fp32 CUDA-core kernel (relu_simt_kernel) instead of tcgen05
 };
 
 // Per (Dp, precision): the TMEM budget is NBUF * BN (x2 for 3xTF32) S columns plus G * Dp Y
@@ -55,12 +56,16 @@ static ProdCfgRt product_cfg(int Dp, bool x3) {
       case 32: return {128, 3, 4, true};
       case 64: return {128, 2, 2, true};
       case 128: return {64, 2, 1, true};
+      case 256: return {32, 1, 1, true};  // tf32 second MMA (no room for an fp16 C copy)
     }
   } else {
     switch (Dp) {
       case 16: return {64, 4, 8, true};
       case 32: return {64, 2, 4, true};
       case 64: return {64, 2, 1, true};
+      case 128: return {32, 1, 1, true};
+      // a 128-row X tile in hi + lo halves is 256 KB at Dp = 256: more than shared memory
+      case 256: return {0, 0, 0, true, true};
     }
   }
   return {0, 0, 0, false};
@@ -81,6 +86,7 @@ static ProdCfgRt reduce_cfg(int Dp, bool x3) {
       case 32: return {128, 3, 4, true};
       case 64: return {64, 3, 2, true};
       case 128: return {32, 2, 1, true};
+      case 256: return {0, 0, 0, true, true};
     }
   }
   return {0, 0, 0, false};
@@ -119,6 +125,7 @@ static void plan_work(int64_t M, int64_t N, int bn, int G, int num_sms, ProductP
 int product_split_count(int64_t M, int64_t N, int Dp, bool x3, int num_sms) {
   ProdCfgRt c = product_cfg(Dp, x3);
   if (!c.ok) return 0;
+  if (c.simt) return 1;
   ProductParams p;
   plan_work(M, N, c.bn, c.g, num_sms, &p);
   return p.splits;
@@ -157,9 +164,11 @@ static int dispatch_product(int Dp, const ProdCfgRt& c, bool x3, const CUtensorM
   SB_PRODUCT_CASE(32, 128, 3, false, false, 4)
   SB_PRODUCT_CASE(64, 128, 2, false, false, 2)
   SB_PRODUCT_CASE(128, 64, 2, false, false, 1)
+  SB_PRODUCT_CASE(256, 32, 1, false, false, 1)
   SB_PRODUCT_CASE(16, 64, 4, true, false, 8)
   SB_PRODUCT_CASE(32, 64, 2, true, false, 4)
   SB_PRODUCT_CASE(64, 64, 2, true, false, 1)
+  SB_PRODUCT_CASE(128, 32, 1, true, false, 1)
   return -1;
 }
 
@@ -184,14 +193,168 @@ static CUtensorMapSwizzle row_swizzle(int Dp) {
   return Dp * 4 >= 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
 }
 
+// ------------------------------------------------------------------------------------------
+// fp32 CUDA-core path for the 3xTF32 (fp32-accurate) mode at Dp = 256, where a 128-row X tile in
+// tf32 hi + lo halves (256 KB) does not fit shared memory. Persistent CTAs of 256 threads take
+// 64-row blocks of X; per 32-row chunk of F: S = X F^T (each thread 8 entries, K = Dp in fp32
+// FMAs from shared memory), R = ReLU(S) to shared memory, then Y += R C (each thread 64 of the
+// block's 64 x Dp outputs in registers) or the (sum R, sum R^2) accumulation. F = Fhi + Flo and
+// C^T = Cthi + Ctlo are reassembled exactly (the halves of a tf32 split add up to the fp32 value).
+template <int DP, bool REDUCE>
+__global__ void __launch_bounds__(256, 1)
+    relu_simt_kernel(const float* __restrict__ X, int M, const float* __restrict__ Fhi,
+                     const float* __restrict__ Flo, int N, const float* __restrict__ Cthi,
+                     const float* __restrict__ Ctlo, int64_t ldct, float* __restrict__ Y,
+                     double* __restrict__ partials, int step) {
+  constexpr int RB = 64, CB = 32, LDS = DP + 4;   // rows per block, chunk rows, padded stride
+  constexpr int YC = DP / 4;                      // output columns per thread
+  extern __shared__ __align__(16) float sm[];
+  float* sX = sm;                        // [RB][LDS]
+  float* sF = sX + RB * LDS;             // [CB][LDS]
+  float* sC = sF + CB * LDS;             // [CB][DP]   (product mode)
+  float* sR = sC + (REDUCE ? 0 : CB * DP);  // [RB][CB + 1]
+  const int t = threadIdx.x;
+  const int r = t >> 2, q = t & 3;
+  double acc_s = 0.0, acc_s2 = 0.0;
+  for (int rb = blockIdx.x; rb * RB < M; rb += gridDim.x) {
+    const int row0 = rb * RB;
+    __syncthreads();
+    for (int i = t; i < RB * DP / 4; i += 256) {
+      const int rr = i / (DP / 4), kk = (i % (DP / 4)) * 4;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (row0 + rr < M) v = *reinterpret_cast<const float4*>(X + (size_t)(row0 + rr) * DP + kk);
+      *reinterpret_cast<float4*>(sX + rr * LDS + kk) = v;
+    }
+    float y[YC];
+#pragma unroll
+    for (int j = 0; j < YC; ++j) y[j] = 0.f;
+    for (int c0 = 0; c0 < N; c0 += CB) {
+      __syncthreads();
+      for (int i = t; i < CB * DP / 4; i += 256) {
+        const int jj = i / (DP / 4), kk = (i % (DP / 4)) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c0 + jj < N) {
+          const float4 h = *reinterpret_cast<const float4*>(Fhi + (size_t)(c0 + jj) * DP + kk);
+          const float4 l = *reinterpret_cast<const float4*>(Flo + (size_t)(c0 + jj) * DP + kk);
+          v = make_float4(h.x + l.x, h.y + l.y, h.z + l.z, h.w + l.w);
+        }
+        *reinterpret_cast<float4*>(sF + jj * LDS + kk) = v;
+      }
+      if constexpr (!REDUCE) {
+        for (int i = t; i < CB * DP; i += 256) {
+          const int k = i / CB, jj = i % CB;
+          float v = 0.f;
+          if (c0 + jj < N) v = Cthi[(size_t)k * ldct + c0 + jj] + Ctlo[(size_t)k * ldct + c0 + jj];
+          sC[jj * DP + k] = v;
+        }
+      }
+      __syncthreads();
+      // S[r][q*8 .. q*8+7]
+      float s[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s[j] = 0.f;
+      for (int k = 0; k < DP; k += 4) {
+        const float4 xv = *reinterpret_cast<const float4*>(sX + r * LDS + k);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float4 fv = *reinterpret_cast<const float4*>(sF + (q * 8 + j) * LDS + k);
+          s[j] = fmaf(xv.x, fv.x, fmaf(xv.y, fv.y, fmaf(xv.z, fv.z, fmaf(xv.w, fv.w, s[j]))));
+        }
+      }
+      if constexpr (REDUCE) {
+        float cs = 0.f, cs2 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const bool valid = row0 + r < M && c0 + q * 8 + j < N;
+          const float v = valid ? fmaxf(s[j], 0.f) : 0.f;
+          cs += v;
+          cs2 = fmaf(v, v, cs2);
+        }
+        acc_s += (double)cs;
+        acc_s2 += (double)cs2;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          sR[r * (CB + 1) + q * 8 + j] = step ? (s[j] > 0.f ? 1.f : 0.f) : fmaxf(s[j], 0.f);
+        __syncthreads();
+        for (int jj = 0; jj < CB; ++jj) {
+          const float rv = sR[r * (CB + 1) + jj];
+          const float* cr = sC + jj * DP + q * YC;
+#pragma unroll
+          for (int j = 0; j < YC; j += 4) {
+            const float4 cv = *reinterpret_cast<const float4*>(cr + j);
+            y[j] = fmaf(rv, cv.x, y[j]);
+            y[j + 1] = fmaf(rv, cv.y, y[j + 1]);
+            y[j + 2] = fmaf(rv, cv.z, y[j + 2]);
+            y[j + 3] = fmaf(rv, cv.w, y[j + 3]);
+          }
+        }
+      }
+    }
+    if constexpr (!REDUCE) {
+      if (row0 + r < M) {
+        float* out = Y + (size_t)(row0 + r) * DP + q * YC;
+#pragma unroll
+        for (int j = 0; j < YC; j += 4)
+          *reinterpret_cast<float4*>(out + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
+      }
+    }
+  }
+  if constexpr (REDUCE) {
+    __shared__ double red[2][8];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      acc_s += __shfl_xor_sync(0xffffffffu, acc_s, o);
+      acc_s2 += __shfl_xor_sync(0xffffffffu, acc_s2, o);
+    }
+    __syncthreads();
+    if ((t & 31) == 0) { red[0][t >> 5] = acc_s; red[1][t >> 5] = acc_s2; }
+    __syncthreads();
+    if (t == 0) {
+      double a = 0.0, b = 0.0;
+      for (int w = 0; w < 8; ++w) { a += red[0][w]; b += red[1][w]; }
+      partials[2 * blockIdx.x] = a;
+      partials[2 * blockIdx.x + 1] = b;
+    }
+  }
+}
+
+template <bool REDUCE>
+static int launch_simt(const float* X, int64_t M, const float* Fhi, const float* Flo, int64_t N,
+                       const float* Cthi, const float* Ctlo, int64_t ldct, float* Y,
+                       double* partials, int num_sms, cudaStream_t stream, int* grid_out,
+                       int step) {
+  constexpr int DP = 256, LDS = DP + 4;
+  constexpr size_t smem = sizeof(float) * (64 * LDS + 32 * LDS + (REDUCE ? 0 : 32 * DP) +
+                                           (REDUCE ? 0 : 64 * 33));
+  auto kern = relu_simt_kernel<DP, REDUCE>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return (int)e;
+    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  }
+  const int64_t blocks = (M + 63) / 64;
+  const int grid = (int)(blocks < num_sms ? blocks : num_sms);
+  if (grid_out) *grid_out = grid;
+  count_launch();
+  kern<<<grid, 256, smem, stream>>>(X, (int)M, Fhi, Flo ? Flo : Fhi, (int)N, Cthi, Ctlo, ldct, Y,
+                                    partials, step);
+  return (int)cudaGetLastError();
+}
+
 int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float* Flo,
                         const float* Cthi, const float* Ctlo, int64_t ldct, int64_t N, int Dp,
                         bool x3, float* ws, int* err, int num_sms, unsigned long long timeout_ns,
-                        cudaStream_t stream, const unsigned int* stats) {
+                        cudaStream_t stream, const unsigned int* stats, int step) {
   ProdCfgRt c = product_cfg(Dp, x3);
   if (!c.ok) return -1;
   if (M <= 0 || N <= 0 || M >= INT32_MAX || N >= INT32_MAX) return -5;
   if (!x3 && !stats) return -7;  // the fp16 second MMA needs the operand maxima
+  if (c.simt) return launch_simt<false>(X, M, Fhi, Flo, N, Cthi, Ctlo, ldct, ws, nullptr, num_sms,
+                                        stream, nullptr, step);
   const uint32_t box_k = Dp * 4 <= 128 ? Dp : 32;
   CUtensorMap mx, mfh, mfl, mch, mcl;
   const CUtensorMapSwizzle sw = row_swizzle(Dp);
@@ -210,6 +373,7 @@ int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float
   p.timeout_ns = timeout_ns;
   p.Xg = X;
   p.stats = stats;
+  p.step = step;
   const int64_t items = (int64_t)p.n_groups * p.splits;
   const int grid = (int)(items < num_sms ? items : num_sms);
   return dispatch_product(Dp, c, x3, mx, mfh, mfl, mch, mcl, p, grid, stream);
@@ -221,6 +385,8 @@ int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float*
   ProdCfgRt c = reduce_cfg(Dp, x3);
   if (!c.ok) return -1;
   if (M <= 0 || N <= 0 || M >= INT32_MAX || N >= INT32_MAX) return -5;
+  if (c.simt) return launch_simt<true>(X, M, Fhi, Flo, N, nullptr, nullptr, 0, nullptr, partials,
+                                       num_sms, stream, grid_out, 0);
   const uint32_t box_k = Dp * 4 <= 128 ? Dp : 32;
   CUtensorMap mx, mfh, mfl;
   const CUtensorMapSwizzle sw = row_swizzle(Dp);
@@ -234,6 +400,7 @@ int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float*
   p.ws = nullptr;
   p.Xg = X;
   p.stats = nullptr;
+  p.step = 0;
   p.partials = partials;
   p.err = err;
   p.timeout_ns = timeout_ns;

@@ -84,6 +84,9 @@ struct ProductParams {
   // Xg is X in global memory (row norms for the per-row scale of R).
   const float* Xg;
   const unsigned int* stats;
+  // product mode: 0 = R = ReLU(S); 1 = R = step(S) (1 where S > 0, else 0), the mask term of the
+  // gradient of sum ReLU(A B^T) (relu_bat_reduce_jit/custom_op.py:74-82)
+  int step;
 };
 
 template <int DP, int BN, int STAGES, bool X3, bool REDUCE, int G>
@@ -107,7 +110,9 @@ struct ProductCfg {
   static constexpr int LOADS_PER_PREC = KSUB + (REDUCE ? 0 : BN / 32);
   static constexpr int NLOADS = NPREC * LOADS_PER_PREC;
   static_assert(NLOADS <= 16, "one producer lane per copy");
-  static constexpr bool H16 = !X3 && !REDUCE;                     // fp16 second MMA
+  // TF32 product mode runs the second MMA in fp16 (half the instructions of kind::tf32) up to
+  // Dp = 128; at Dp = 256 the stage has no room for the fp16 copy of C, and R stays fp32 (tf32)
+  static constexpr bool H16 = !X3 && !REDUCE && DP <= 128;        // fp16 second MMA
   static constexpr int C16_BYTES = H16 ? DP * BN * 2 : 0;         // fp16 copy of the C chunk
   static constexpr int STAGE_ALLOC = STAGE_BYTES + C16_BYTES;
   static constexpr int XBUF_BYTES = NPREC * X_BYTES;      // one X slot (hi [, lo])
@@ -134,7 +139,14 @@ struct ProductCfg {
       (1u << 4) | ((uint32_t)(DP >> 3) << 17) | ((uint32_t)(TM >> 4) << 24);
   static constexpr int EPI_WARPS = 8;                     // two per TMEM lane quadrant
   static constexpr int EPI_THREADS = 32 * EPI_WARPS;
-  static constexpr bool AUX = X3 || H16;                  // warp 10: X splitter / C converter
+  // TF32 mode rounds every operand to the nearest tf32 value in shared memory before the tensor
+  // core reads it (the tensor core itself would drop the low 13 mantissa bits, a bias of about
+  // -2^-12 per operand): the X tiles by the epilogue warps when a group starts, each (F, C) chunk
+  // by the chunk-prep warp, which in product mode also builds the fp16 copy of C
+  static constexpr bool ROUND = !X3;
+  static constexpr bool AUX = X3 || !REDUCE;              // warp 10: X splitter / chunk prep
+  static constexpr int CPREP_WARP = REDUCE ? 11 : 10;     // chunk-prep warp (ROUND)
+  static_assert(!H16 || BN % 64 == 0, "the fp16 C chunk is built of 64-element sub-tiles");
   // product mode: second-MMA issuers, warp MMA2_WARP + i takes the tiles gi with gi % N2 == i
   static constexpr int MMA2_WARP = 11;
   static constexpr int N2 = 2;
@@ -154,7 +166,7 @@ struct ProductCfg {
   // issuer's pairs are N1 apart, so N1 <= NBUF suffices.
   static_assert(REDUCE ? N1 <= NBUF : (N1 == 1 && NBUF >= 2 * N2 - 1), "barrier phase lag");
   static constexpr int THREADS =
-      REDUCE ? 32 * (N1 == 2 ? 11 : 10 + (AUX ? 1 : 0)) : 32 * (MMA2_WARP + N2);
+      REDUCE ? 32 * (X3 ? 11 : 12) : 32 * (MMA2_WARP + N2);
   // mbarriers, TMEM slot and abort flag sit below the epilogue's reduction scratch at +768 B
   static_assert((3 * STAGES + 3 * NBUF + 5 * G + N1 + N2) * 8 + 8 <= 768, "barrier area");
   static constexpr int EPI_COLS = BN / 2;                 // S columns per epilogue warp
@@ -185,6 +197,21 @@ __device__ __forceinline__ int chunk_at(const WorkItem& w, int ci) {
   return w.c0 + (int)((ci + blockIdx.x) % (unsigned)nc);
 }
 
+// Round NV 16-byte units of shared memory at `base` in place, unit i by thread i % NT.
+template <int NV, int NT>
+__device__ __forceinline__ void round_tf32_smem(uint8_t* base, int t) {
+  uint4* q = reinterpret_cast<uint4*>(base);
+#pragma unroll 4
+  for (int i = t; i < NV; i += NT) {
+    uint4 v = q[i];
+    v.x = tf32_rne_bits(v.x);
+    v.y = tf32_rne_bits(v.y);
+    v.z = tf32_rne_bits(v.z);
+    v.w = tf32_rne_bits(v.w);
+    q[i] = v;
+  }
+}
+
 // fp16x2 of (ReLU(lo), ReLU(hi)), round to nearest; lo in the low half.
 __device__ __forceinline__ uint32_t pack_relu_h2(float lo, float hi) {
   uint32_t r;
@@ -209,12 +236,12 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::SMEM_DATA);
   uint64_t* full = bars;                    // [STAGES] TMA landed
   uint64_t* empty = full + STAGES;          // [STAGES] last MMA reading the stage completed
-  uint64_t* c16_ready = empty + STAGES;     // [STAGES] fp16 C chunk converted (H16)
+  uint64_t* c16_ready = empty + STAGES;     // [STAGES] chunk rounded / C converted (ROUND)
   uint64_t* s_full = c16_ready + STAGES;    // [NBUF] S = X F^T computed
   uint64_t* r_ready = s_full + NBUF;        // [NBUF] epilogue done with the S buffer
   uint64_t* s_free = r_ready + NBUF;        // [NBUF] second MMA done with the S buffer
   uint64_t* x_full = s_free + NBUF;         // [G] X slot landed
-  uint64_t* x_ready = x_full + G;           // [G] X slot split (3xTF32)
+  uint64_t* x_ready = x_full + G;           // [G] X slot split (3xTF32) or rounded (TF32)
   uint64_t* x_empty = x_ready + G;          // [G] last MMA reading the X slot completed
   uint64_t* y_full = x_empty + G;           // [G] Y accumulator complete
   uint64_t* y_empty = y_full + G;           // [G] Y accumulator read out
@@ -240,7 +267,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
     }
     for (int g = 0; g < G; ++g) {
       mbar_init(&x_full[g], 1);
-      mbar_init(&x_ready[g], 32);
+      mbar_init(&x_ready[g], X3 ? 32 : Cfg::EPI_THREADS);
       mbar_init(&x_empty[g], Cfg::N1);
       mbar_init(&y_full[g], 1);
       mbar_init(&y_empty[g], Cfg::EPI_THREADS);
@@ -349,13 +376,13 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
         // slots' release barrier (one commit per issuer) must not see a commit for this group
         // before the previous group's phase has completed
         for (int gi = 0; gi < w.ntiles && ok; ++gi)
-          if (!mbar_wait(X3 ? &x_ready[gi] : &x_full[gi], (slot_par >> gi) & 1u, abort_flag,
+          if (!mbar_wait(&x_ready[gi], (slot_par >> gi) & 1u, abort_flag,
                          p.err, DEV_TIMEOUT_X, p.timeout_ns)) ok = false;
         for (int ci = 0; ci < w.c1 - w.c0 && ok; ++ci, ++chunk) {
           const int c = chunk_at(w, ci);
           const int stage = chunk % STAGES;
-          if (!mbar_wait(&full[stage], (chunk / STAGES) & 1, abort_flag, p.err, DEV_TIMEOUT_FULL,
-                         p.timeout_ns)) { ok = false; break; }
+          if (!mbar_wait(Cfg::ROUND ? &c16_ready[stage] : &full[stage], (chunk / STAGES) & 1,
+                         abort_flag, p.err, DEV_TIMEOUT_FULL, p.timeout_ns)) { ok = false; break; }
           const uint32_t fbase = sSt_addr + stage * Cfg::STAGE_ALLOC;
           for (int gi = 0; gi < w.ntiles; ++gi, ++pair) {
             if ((int)(pair % Cfg::N1) != me1) continue;
@@ -423,7 +450,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           const uint32_t stg = sSt_addr + stage * Cfg::STAGE_ALLOC;
           // every issuer waits for the chunk, even one that owns no tile of this group: its
           // commit on `empty` below must not run ahead into a later phase of the barrier
-          if (!mbar_wait(Cfg::H16 ? &c16_ready[stage] : &full[stage], (chunk / STAGES) & 1,
+          if (!mbar_wait(Cfg::ROUND ? &c16_ready[stage] : &full[stage], (chunk / STAGES) & 1,
                          abort_flag, p.err, DEV_TIMEOUT_FULL, p.timeout_ns)) { ok = false; break; }
           for (int gi = 0; gi < w.ntiles; ++gi, ++pair) {
             if (gi % Cfg::N2 != me) continue;
@@ -506,6 +533,18 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
     }
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const WorkItem w = work_item(p, item);
+      if constexpr (Cfg::ROUND) {
+        // round the group's X tiles to tf32 in place before the first MMA reads them
+        for (int gi = 0; gi < w.ntiles && ok; ++gi) {
+          if (!mbar_wait(&x_full[gi], (slot_par >> gi) & 1u, abort_flag, p.err, DEV_TIMEOUT_X,
+                         p.timeout_ns)) { ok = false; break; }
+          round_tf32_smem<Cfg::X_BYTES / 16, Cfg::EPI_THREADS>(sX + gi * Cfg::XBUF_BYTES,
+                                                               threadIdx.x - 64);
+          fence_proxy_async_smem();
+          mbar_arrive(&x_ready[gi]);
+        }
+        if (!ok) break;
+      }
       int er[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) er[g] = 0;
@@ -525,7 +564,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
             const float bound = sqrtf(n2) * fmax * 1.001f;
             int ex = 0;
             if (bound > 0.f) frexpf(bound, &ex);
-            er[g] = 14 - ex;
+            er[g] = p.step ? 0 : 14 - ex;  // step values are 0 or 1: no scale needed
           }
         }
       }
@@ -564,9 +603,9 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
               float lo[Cfg::LDW];
 #pragma unroll
               for (int i = 0; i < Cfg::LDW; ++i) {
-                const float r = fmaxf(v[col + i], 0.f);
+                const float r = p.step ? (v[col + i] > 0.f ? 1.f : 0.f) : fmaxf(v[col + i], 0.f);
                 const float h = tf32_hi(r);
-                lo[i] = r - h;
+                lo[i] = tf32_lo(r, h);
                 v[col + i] = h;
               }
               if constexpr (Cfg::LDW == 32) {
@@ -578,14 +617,31 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
               }
             }
             tmem_st_wait();
+          } else if constexpr (!Cfg::H16) {
+            // plain TF32 second MMA: R = ReLU(S) in place (the tensor core reads it as tf32)
+#pragma unroll
+            for (int col = 0; col < Cfg::EPI_COLS; col += Cfg::LDW) {
+#pragma unroll
+              for (int i = 0; i < Cfg::LDW; ++i)
+                v[col + i] = p.step ? (v[col + i] > 0.f ? 1.f : 0.f) : fmaxf(v[col + i], 0.f);
+              if constexpr (Cfg::LDW == 32) tmem_st32(s_tm + col, v + col);
+              else tmem_st16(s_tm + col, v + col);
+            }
+            tmem_st_wait();
           } else {
             // pack ReLU(R) (scaled) as fp16 pairs (even k in the low half) into this warp's own
             // first EPI_COLS / 2 columns
             const float rscale = __int_as_float((127 + er[gi]) << 23);
             uint32_t pk[Cfg::EPI_COLS / 2];
+            if (p.step) {
 #pragma unroll
-            for (int i = 0; i < Cfg::EPI_COLS / 2; ++i)
-              pk[i] = pack_relu_h2(v[2 * i] * rscale, v[2 * i + 1] * rscale);
+              for (int i = 0; i < Cfg::EPI_COLS / 2; ++i)
+                pk[i] = (v[2 * i] > 0.f ? 0x3C00u : 0u) | (v[2 * i + 1] > 0.f ? 0x3C000000u : 0u);
+            } else {
+#pragma unroll
+              for (int i = 0; i < Cfg::EPI_COLS / 2; ++i)
+                pk[i] = pack_relu_h2(v[2 * i] * rscale, v[2 * i + 1] * rscale);
+            }
             if constexpr (Cfg::EPI_COLS / 2 == 32) tmem_st32(s_tm, reinterpret_cast<const float*>(pk));
             else tmem_st16(s_tm, reinterpret_cast<const float*>(pk));
             tmem_st_wait();
@@ -646,14 +702,18 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
         p.partials[2 * blockIdx.x + 1] = b;
       }
     }
-  } else if (Cfg::H16 && warp == 2 + Cfg::EPI_WARPS) {
+  } else if (Cfg::ROUND && warp == Cfg::CPREP_WARP) {
+    if constexpr (Cfg::ROUND) {
+    // ------------------------------------------------------------------ chunk prep (TF32 mode)
+    // rounds the F chunk to tf32 in place; product mode: fp32 C chunk (32-float SW128 sub-tiles)
+    // -> fp16 scaled by 2^ec (64-element SW128 sub-tiles), or (Dp = 256) C rounded in place
+    float cscale = 1.f;
     if constexpr (Cfg::H16) {
-    // ------------------------------------------------------------------ C converter (warp 10)
-    // fp32 C chunk (32-float SW128 sub-tiles) -> fp16, scaled by 2^ec (64-element SW128 sub-tiles)
-    const float cmax = __uint_as_float(p.stats[1]);
-    int ex = 0;
-    if (cmax > 0.f) frexpf(cmax, &ex);
-    const float cscale = ldexpf(1.f, 14 - ex);
+      const float cmax = __uint_as_float(p.stats[1]);
+      int ex = 0;
+      if (cmax > 0.f) frexpf(cmax, &ex);
+      cscale = ldexpf(1.f, 14 - ex);
+    }
     uint32_t gch = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
@@ -665,8 +725,12 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           ok = false;
           break;
         }
-        const uint8_t* src = sStage + stage * Cfg::STAGE_ALLOC + Cfg::F_BYTES;
-        uint8_t* dst = sStage + stage * Cfg::STAGE_ALLOC + Cfg::STAGE_BYTES;
+        uint8_t* stg = sStage + stage * Cfg::STAGE_ALLOC;
+        round_tf32_smem<Cfg::F_BYTES / 16, 32>(stg, lane);
+        if constexpr (!REDUCE && !Cfg::H16) round_tf32_smem<Cfg::C_BYTES / 16, 32>(stg + Cfg::F_BYTES, lane);
+        if constexpr (Cfg::H16) {
+        const uint8_t* src = stg + Cfg::F_BYTES;
+        uint8_t* dst = stg + Cfg::STAGE_BYTES;
         constexpr int UNITS = (BN / 64) * DP * 8;  // 16-byte fp16 units
         static_assert(UNITS % 32 == 0, "whole rounds of the converter warp");
         // batches of UB units per lane: all loads of a batch are issued before its stores, so
@@ -703,6 +767,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
                 *reinterpret_cast<const uint4*>(h);
           }
         }
+        }
         fence_proxy_async_smem();
         mbar_arrive(&c16_ready[stage]);
         if (lane == 0) SB_TR(11, gch);
@@ -724,7 +789,8 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           const float4 v = xs[i];
           const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
           xs[i] = h;
-          xl[i] = make_float4(v.x - h.x, v.y - h.y, v.z - h.z, v.w - h.w);
+          xl[i] = make_float4(tf32_lo(v.x, h.x), tf32_lo(v.y, h.y), tf32_lo(v.z, h.z),
+                              tf32_lo(v.w, h.w));
         }
         fence_proxy_async_smem();
         mbar_arrive(&x_ready[gi]);

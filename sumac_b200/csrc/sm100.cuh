@@ -281,4 +281,19 @@ __device__ __forceinline__ float tf32_hi(float x) {
   return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
 }
 
+// Round an fp32 bit pattern to the nearest tf32 value (ties to even), keeping it in fp32 form with
+// the low 13 mantissa bits zero; Inf and NaN pass through (a finite value can round up to Inf).
+__device__ __forceinline__ uint32_t tf32_rne_bits(uint32_t u) {
+  if ((u & 0x7f800000u) == 0x7f800000u) return u;
+  u += 0xfffu + ((u >> 13) & 1u);
+  return u & 0xffffe000u;
+}
+
+// Low half of the 3xTF32 split x = hi + lo with hi = tf32_hi(x): the remainder x - hi (exact in
+// fp32) rounded to the nearest tf32 value, so that the tensor core, which drops the low 13 bits
+// of an fp32 operand, reads it without a one-sided truncation error.
+__device__ __forceinline__ float tf32_lo(float x, float hi) {
+  return __uint_as_float(tf32_rne_bits(__float_as_uint(x - hi)));
+}
+
 }  // namespace sb

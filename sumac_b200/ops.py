@@ -49,8 +49,12 @@ def pad_factor(F: torch.Tensor, Dp: int | None = None) -> torch.Tensor:
 
 
 # ------------------------------------------------------------------ reference ops
-def relu_bat_c(A, B, C, precision=SUMAC_3XTF32):
-    """Y = ReLU(B A^T) C with A[N, D], B[M, D], C[N, D] (relu_bat_c_base.py:4-6)."""
+SUMAC_RELU, SUMAC_STEP = 0, 1
+
+
+def relu_bat_c(A, B, C, precision=SUMAC_3XTF32, mode=SUMAC_RELU):
+    """Y = ReLU(B A^T) C with A[N, D], B[M, D], C[N, D] (relu_bat_c_base.py:4-6); with
+    mode=SUMAC_STEP, Y = step(B A^T) C (1 where B A^T > 0, else 0)."""
     A, B, C = _cuda_f32("A", A), _cuda_f32("B", B), _cuda_f32("C", C)
     Nr, D = A.shape
     M, DB = B.shape
@@ -66,8 +70,9 @@ def relu_bat_c(A, B, C, precision=SUMAC_3XTF32):
     if nb == 0:
         raise NotImplementedError(f"relu_bat_c: D={D} not supported")
     ws = _ws(A.device, nb)
-    check(L.sumac_relu_bat_c(ptr(A), ptr(B), ptr(C), M, Nr, D, ptr(Y), precision, ptr(ws), ws.numel(),
-                             ptr(N.err_word(A.device)), N.stream_ptr(A.device)), "relu_bat_c")
+    check(L.sumac_relu_bat_c_mode(ptr(A), ptr(B), ptr(C), M, Nr, D, ptr(Y), precision, int(mode),
+                                  ptr(ws), ws.numel(), ptr(N.err_word(A.device)),
+                                  N.stream_ptr(A.device)), "relu_bat_c")
     return Y
 
 

@@ -31,13 +31,16 @@ def refactor(A: Tensor, B: Tensor) -> tuple[Tensor, Tensor]:
 
 def init_salsa_factors(S_index, S_value, m, n, d, gen):
     """A > 0, B < 0 from S times uniform noise, rescaled, then refactored
-    (training/salsa.py:36-78); draws from `gen` in the same order as the reference."""
+    (training/salsa.py:36-78); draws from `gen` in the same order as the reference. The uniform
+    draws come from `gen` on its own device; the arithmetic runs on the device of S_value. The
+    steps (sparse products, closed-form scale, QR + QR + SVD) are the reference's, in its order: the
+    same draws in the same order are what makes the initial factors match a reference run."""
     device, dtype = S_value.device, S_value.dtype
     with torch.sparse.check_sparse_tensor_invariants(False):
         S = torch.sparse_coo_tensor(S_index.to(device=device, dtype=torch.long), S_value,
                                     size=(m, n), device=device, dtype=dtype).coalesce()
-        R_A = torch.rand((n, d), device=device, dtype=dtype, generator=gen)
-        R_B = torch.rand((m, d), device=device, dtype=dtype, generator=gen)
+        R_A = torch.rand((n, d), device=gen.device, dtype=dtype, generator=gen).to(device)
+        R_B = torch.rand((m, d), device=gen.device, dtype=dtype, generator=gen).to(device)
         A = torch.sqrt(torch.sparse.mm(S, R_A))
         B = -torch.sqrt(torch.sparse.mm(S.T, R_B))
     Lij = torch.sum(A[S_index[0], :] * B[S_index[1], :], dim=1)

@@ -186,6 +186,31 @@ def end_to_end():
          jacc=hist["jacc"])
 
 
+def c1_planted():
+    """the planted 2000 x 1500 problem (bench.make_c1, deterministic numpy),
+    GD with rank 8 for 50 iterations from the reference's own initialisation (no A_init/B_init),
+    seed 0, on the CPU. The data are regenerated by the tests from bench.make_c1; the fixture keeps
+    their size and checksum, the reference's initial factors (init_salsa_factors with the seed-0
+    generator, as GD_loop draws them) and the run's history and final factors."""
+    sys.path.insert(0, os.path.dirname(os.path.dirname(OUT)))
+    from bench import make_c1
+    from sumac.training.salsa import init_salsa_factors
+    idx_np, val_np, (m, n) = make_c1()
+    idx = torch.from_numpy(idx_np)
+    vals = torch.from_numpy(val_np)
+    assert torch.unique(idx[0]).numel() == m and torch.unique(idx[1]).numel() == n  # nothing pruned
+    d, iters = 8, 50
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    A0, B0 = init_salsa_factors(idx, vals, m, n, d, gen)
+    cfg = SumacConfig(method=SumacMethod.GD, rank=d, max_iterations=iters, eval_interval=10,
+                      seed=0, verbose=False, autotune=AutotuneMode.DISABLE,
+                      device=torch.device("cpu"))
+    A, B, hist = sumac_factorize(S_index=idx, S_value=vals, shape=(m, n), config=cfg)
+    save("c1_gd", m=m, n=n, rank=d, iters=iters, seed=0, nnz=vals.numel(),
+         value_sum=vals.double().sum(), A0=A0, B0=B0, A=A, B=B, cost=hist["cost"],
+         rmse=hist["rmse"], jacc=hist["jacc"])
+
+
 if __name__ == "__main__":
     torch.set_num_threads(4)
     kernels()
@@ -193,4 +218,5 @@ if __name__ == "__main__":
     partition()
     metrics_and_gd_grad()
     end_to_end()
+    c1_planted()
     print("golden fixtures written to", OUT, "with torch", torch.__version__)

@@ -10,6 +10,27 @@ def rel_err(got, ref):
     return float(np.abs(got - ref).max() / scale)
 
 
+def assert_close_elementwise(got, ref, rtol, atol_frac):
+    """Every element: |got - ref| <= rtol |ref| + atol_frac max|ref| (a per-element relative bound
+    with an absolute floor tied to the scale of the result)."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    scale = max(np.abs(ref).max(), 1e-30)
+    bound = rtol * np.abs(ref) + atol_frac * scale
+    bad = np.abs(got - ref) > bound
+    assert not bad.any(), (f"{int(bad.sum())} of {bad.size} elements out of tolerance; worst excess "
+                           f"{float((np.abs(got - ref) / bound).max()):.3g}x the bound")
+
+
+def align_column_signs(A, B, A_ref):
+    """Factors are defined up to the sign of each rank-one term (A[:, k], B[:, k]) -> (-A[:, k],
+    -B[:, k]): the SVD in the refactoring step may pick either sign. Flip the columns of A and B
+    whose A column points away from the reference's."""
+    s = np.sign(np.sum(np.asarray(A, np.float64) * np.asarray(A_ref, np.float64), axis=0))
+    s[s == 0] = 1.0
+    return np.asarray(A) * s, np.asarray(B) * s
+
+
 def random_edges(rng, n_fixed, n_out, nnz):
     """Distinct (fixed, out) pairs with positive values."""
     keys = rng.choice(n_fixed * n_out, size=nnz, replace=False)

@@ -10,7 +10,7 @@ import torch
 import torch.nn.functional as F
 
 from sumac_b200 import OptimizerName, SumacConfig, SumacMethod, sumac_factorize
-from tests.helpers import rel_err
+from tests.helpers import align_column_signs, rel_err
 
 pytestmark = pytest.mark.gpu
 
@@ -93,3 +93,50 @@ def test_gd_other_optimizers_run(golden, opt):
     g = golden("e2e_gd")
     A, B, hist = _run(g, SumacMethod.GD, eval_interval=2, batch_blocks=2, optimizer=opt)
     assert np.isfinite(A.cpu().numpy()).all() and len(hist["cost"]) == 2
+
+
+def _c1():
+    from bench import make_c1
+    idx, vals, (m, n) = make_c1()
+    return torch.from_numpy(idx), torch.from_numpy(vals), m, n
+
+
+def test_c1_data_regenerates_exactly(golden):
+    g = golden("c1_gd")
+    idx, vals, m, n = _c1()
+    assert vals.numel() == int(g["nnz"])
+    assert float(vals.double().sum()) == float(g["value_sum"])
+
+
+def test_c1_init_matches_reference(golden):
+    """init_salsa_factors (training/salsa.py:36-78) on the GPU, with the uniform draws from the
+    seed-0 CPU generator the reference's CPU run used: same initial factors up to column signs."""
+    from sumac_b200.salsa import init_salsa_factors
+    g = golden("c1_gd")
+    idx, vals, m, n = _c1()
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    A0, B0 = init_salsa_factors(idx.cuda(), vals.cuda(), m, n, int(g["rank"]), gen)
+    A0, B0 = align_column_signs(A0.cpu().numpy(), B0.cpu().numpy(), g["A0"])
+    assert rel_err(A0, g["A0"]) < 1e-4
+    assert rel_err(B0, g["B0"]) < 1e-4
+
+
+@pytest.mark.parametrize("allow_tf32", [False, True])
+def test_c1_gd_matches_reference_run(golden, allow_tf32):
+    """BASELINE config C1 end to end: GD, rank 8, 50 iterations from the default initialisation,
+    seed 0, against the reference's own CPU run. fp32-accurate mode (the reference's default):
+    history within 1e-4 relative; TF32 mode: history within 1e-3 relative (the north star's
+    bound). Factors up to column signs."""
+    g = golden("c1_gd")
+    idx, vals, m, n = _c1()
+    cfg = SumacConfig(method=SumacMethod.GD, rank=int(g["rank"]), max_iterations=int(g["iters"]),
+                      eval_interval=10, seed=0, verbose=False, perm_device="cpu",
+                      allow_tf32=allow_tf32)
+    A, B, hist = sumac_factorize(S_index=idx.cuda(), S_value=vals.cuda(), shape=(m, n),
+                                 config=cfg)
+    tol = 1e-3 if allow_tf32 else 1e-4
+    for key in ("cost", "rmse", "jacc"):
+        np.testing.assert_allclose(hist[key], g[key], rtol=tol)
+    A, B = align_column_signs(A.cpu().numpy(), B.cpu().numpy(), g["A"])
+    assert rel_err(A, g["A"]) < (1e-2 if allow_tf32 else 1e-3)
+    assert rel_err(B, g["B"]) < (1e-2 if allow_tf32 else 1e-3)
