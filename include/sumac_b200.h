@@ -175,6 +175,14 @@ int sumac_eval_terms(const float* A, const float* B, int64_t m, int64_t n, int d
                      const int32_t* ei, const int32_t* ej, const float* v, int64_t nnz,
                      double* out, int precision, void* ws, size_t ws_bytes, int* dev_err,
                      sumac_stream_t stream);
+/* The eight terms of sumac_eval_terms plus out[8] = the number of positive entries of A B^T,
+ * the numerator of the MATLAB implementation's fnnz = nnz(ReLU(A B^T)) / nnz(S)
+ * (matlab/sumac/compute_errors.m:62, counted by src/sumac/kernels/relu_bat_reduce_jit/
+ * kernel_nnz.cu:11-119). out has 9 doubles; same workspace as sumac_eval_terms. */
+int sumac_eval_terms_fnnz(const float* A, const float* B, int64_t m, int64_t n, int d,
+                          const int32_t* ei, const int32_t* ej, const float* v, int64_t nnz,
+                          double* out, int precision, void* ws, size_t ws_bytes, int* dev_err,
+                          sumac_stream_t stream);
 /* The same eight terms for one GD row block (rows of A, support by column as in
  * sumac_gd_block_grad); out (+)= when accumulate. */
 size_t sumac_block_loss_workspace_bytes(int64_t n, int64_t b_max, int d, int precision);

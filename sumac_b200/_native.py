@@ -56,6 +56,7 @@ _SIGS = {
                                   p, p]),
     "sumac_eval_terms_workspace_bytes": (sz, [i64, i64, i64, i32, i32]),
     "sumac_eval_terms": (i32, [p, p, i64, i64, i32, p, p, p, i64, p, i32, p, sz, p, p]),
+    "sumac_eval_terms_fnnz": (i32, [p, p, i64, i64, i32, p, p, p, i64, p, i32, p, sz, p, p]),
     "sumac_block_loss_workspace_bytes": (sz, [i64, i64, i32, i32]),
     "sumac_block_loss_terms": (i32, [p, p, i64, i32, p, i64, p, p, p, i32, i32, p, sz, p, p]),
     "sumac_adam_step": (i32, [p, p, p, p, i64, f32, f32, f32, f32, f32, p]),

@@ -56,6 +56,10 @@ class SumacConfig:
         on the training device.
       tf32_mode: None (follow allow_tf32: TF32 if True, 3xTF32 fp32-accurate otherwise), or one of
         "tf32", "3xtf32".
+      keep_best: SALSA returns the evaluated iterate of lowest cost, refactored (the MATLAB
+        implementation's finish, matlab/sumac/salsa_loop.m:61-79), instead of the last iterate.
+      report_fnnz: SALSA adds "fnnz" to the history: the fraction nnz(ReLU(A B^T)) / nnz(S) that
+        the MATLAB implementation reports (matlab/sumac/compute_errors.m:62).
     """
     method: SumacMethod = SumacMethod.SALSA
     rank: int = 16
@@ -84,6 +88,8 @@ class SumacConfig:
     # opt-in extensions
     perm_device: str | torch.device | None = None
     tf32_mode: str | None = None
+    keep_best: bool = False
+    report_fnnz: bool = False
 
     def __post_init__(self):
         self._validate_integer_options()

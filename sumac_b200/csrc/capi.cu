@@ -4,6 +4,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 
 #include "../../include/sumac_b200.h"
@@ -80,6 +81,32 @@ int num_sms_current() {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Per device: a side stream and two events that fork work off the caller's stream and join it
+// back (stream-ordered, so it is captured into CUDA graphs as a parallel branch). Created on the
+// first use on a device; SALSA runs its first iteration eagerly, so creation precedes capture.
+struct SideStream {
+  cudaStream_t stream = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+};
+std::mutex g_side_mutex;
+SideStream g_side[64];
+
+SideStream* side_stream() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_side_mutex);
+  SideStream& ss = g_side[dev];
+  if (!ss.stream) {
+    if (cudaStreamCreateWithFlags(&ss.stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ss.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&ss.join, cudaEventDisableTiming) != cudaSuccess) {
+      ss = SideStream{};
+      return nullptr;
+    }
+  }
+  return &ss;
+}
 int64_t round4(int64_t x) { return (x + 3) & ~int64_t(3); }
 
 }  // namespace
@@ -302,7 +329,7 @@ int sumac_masked_product(const float* X, const float* F, const float* C, int64_t
 
 // ------------------------------------------------------------------------------ SALSA update
 struct SalsaPlan {
-  float *FI, *Fhi, *Flo, *P, *Cthi, *Ctlo, *part;
+  float *FI, *Fhi, *Flo, *P, *Cthi, *Ctlo, *part, *ginv;
   double* gram;
   unsigned int* counter;
   int64_t ldct;
@@ -319,8 +346,10 @@ static SalsaPlan plan_salsa(void* ws, int64_t M, int64_t b, int d, int Dp, bool 
   p.Cthi = bp.take<float>((size_t)Dp * p.ldct);
   p.Ctlo = x3 ? bp.take<float>((size_t)Dp * p.ldct) : nullptr;
   const size_t gbytes = (size_t)gram_parts(b) * d * d * sizeof(double);
-  const size_t pbytes = salsa_prep_scratch_bytes(b, d);
+  size_t pbytes = salsa_prep_scratch_bytes(b, d);
+  if (d <= 32 && salsa_ginv_scratch_bytes(b, d) > pbytes) pbytes = salsa_ginv_scratch_bytes(b, d);
   p.gram = bp.take<double>(((gbytes > pbytes ? gbytes : pbytes) + 7) / 8);
+  p.ginv = bp.take<float>((size_t)Dp * Dp);
   p.counter = bp.take<unsigned int>(64);  // [0] done-CTA counter, [1..2] operand maxima
   // the split count grows as b shrinks; size for the worst case over b' <= b
   int smax = 1;
@@ -350,8 +379,9 @@ int sumac_salsa_block_update(const float* F, int64_t m_fixed, const int64_t* row
   if (b <= 0 || M <= 0 || m_fixed <= 0) return fail(SUMAC_ERR_ARG, "salsa_block_update: empty shape");
   if (!F || !rows || !X || !dX || !unbias || !dev_err || (rowptr && !ent))
     return fail(SUMAC_ERR_ARG, "salsa_block_update: null pointer");
-  if (!Dp || !product_supported(Dp, x3))
-    return fail(SUMAC_ERR_UNSUPPORTED, "salsa_block_update: rank %d not supported with precision %d", d, precision);
+  // the solve of the least-squares map keeps the d x d Gram matrix (fp64) in shared memory
+  if (!Dp || d > 128 || !product_supported(Dp, x3))
+    return fail(SUMAC_ERR_UNSUPPORTED, "salsa_block_update: rank %d not supported with precision %d (SALSA takes rank <= 128)", d, precision);
   if (!aligned16(F) || !aligned16(X) || !aligned16(dX))
     return fail(SUMAC_ERR_ARG, "salsa_block_update: factors must be 16-byte aligned");
   const int sms = num_sms_current();
@@ -359,6 +389,30 @@ int sumac_salsa_block_update(const float* F, int64_t m_fixed, const int64_t* row
   if (!ws || ws_bytes < p.bytes)
     return fail(SUMAC_ERR_WORKSPACE, "salsa_block_update: workspace %zu < %zu", ws_bytes, p.bytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (d <= 32) {
+    // C = F_I: the product and the support term contract with the gathered rows themselves and
+    // the finalize pass applies G^{-1}, which a side stream computes while the product runs
+    SideStream* side = side_stream();
+    if (!side) return fail(SUMAC_ERR_CUDA, "salsa_block_update: side stream creation failed");
+    cudaMemsetAsync(p.counter, 0, 3 * sizeof(unsigned int), s);
+    launch_salsa_gather(F, rows, b, Dp, p.FI, p.Fhi, p.Flo, p.Cthi, p.Ctlo, p.ldct,
+                        x3 ? nullptr : p.counter + 1, s);
+    cudaEventRecord(side->fork, s);
+    cudaStreamWaitEvent(side->stream, side->fork, 0);
+    launch_salsa_ginv(p.FI, b, d, Dp, p.gram, p.counter, p.ginv, dev_err, side->stream);
+    cudaEventRecord(side->join, side->stream);
+    int rc = launch_relu_product(X, M, x3 ? p.Fhi : p.FI, p.Flo, p.Cthi, p.Ctlo, p.ldct, b, Dp,
+                                 x3, p.part, dev_err, sms, g_timeout_ns, s, p.counter + 1);
+    cudaStreamWaitEvent(s, side->join, 0);
+    if (rc) return cuda_status(rc, "salsa_block_update");
+    FinalizeArgs f{};
+    f.mode = FIN_SALSA; f.M = M; f.Dp = Dp; f.splits = product_split_count(M, b, Dp, x3, sms);
+    f.ws = p.part; f.X = X; f.dX = dX; f.F = p.FI; f.Cm = p.FI; f.ginv = p.ginv;
+    f.rowptr = rowptr; f.ent = reinterpret_cast<const int2*>(ent);
+    f.momentum = momentum; f.lrate = lrate; f.unbias = unbias;
+    launch_finalize(f, s);
+    return launched("salsa_block_update");
+  }
   if (d <= 32) {
     cudaMemsetAsync(p.counter, 0, 3 * sizeof(unsigned int), s);
     launch_salsa_prep(F, rows, b, d, Dp, p.FI, p.Fhi, p.Flo, p.P, p.Cthi, p.Ctlo, p.ldct, p.gram,
@@ -502,7 +556,7 @@ static EvalPlan plan_eval(void* ws, int64_t nf, int64_t nsparse, int Dp, bool x3
   EvalPlan p;
   p.Fhi = x3 ? bp.take<float>((size_t)nf * Dp) : nullptr;
   p.Flo = x3 ? bp.take<float>((size_t)nf * Dp) : nullptr;
-  p.red = bp.take<double>((size_t)sms * 2);
+  p.red = bp.take<double>((size_t)sms * 3 + 3);
   p.sp = bp.take<double>((size_t)sparse_terms_grid(nsparse) * 6);
   p.bytes = bp.off + 256;
   return p;
@@ -514,10 +568,10 @@ size_t sumac_eval_terms_workspace_bytes(int64_t m, int64_t n, int64_t nnz, int d
   return plan_eval(nullptr, m < n ? m : n, nnz, Dp, precision == SUMAC_3XTF32, num_sms_current()).bytes;
 }
 
-int sumac_eval_terms(const float* A, const float* B, int64_t m, int64_t n, int d,
-                     const int32_t* ei, const int32_t* ej, const float* v, int64_t nnz,
-                     double* out, int precision, void* ws, size_t ws_bytes, int* dev_err,
-                     sumac_stream_t stream) {
+static int eval_terms_impl(const float* A, const float* B, int64_t m, int64_t n, int d,
+                           const int32_t* ei, const int32_t* ej, const float* v, int64_t nnz,
+                           double* out, int precision, void* ws, size_t ws_bytes, int* dev_err,
+                           sumac_stream_t stream, bool count) {
   const bool x3 = precision == SUMAC_3XTF32;
   const int Dp = padded(d);
   if (m <= 0 || n <= 0 || nnz < 0) return fail(SUMAC_ERR_ARG, "eval_terms: empty shape");
@@ -536,13 +590,37 @@ int sumac_eval_terms(const float* A, const float* B, int64_t m, int64_t n, int d
   if (x3) launch_gather_pad(F, Dp, Dp, nullptr, NF, Dp, nullptr, p.Fhi, p.Flo, s);
   int grid = 0;
   int rc = launch_relu_reduce(X, MX, x3 ? p.Fhi : F, p.Flo, NF, Dp, x3, p.red, &grid, dev_err, sms,
-                              g_timeout_ns, s);
+                              g_timeout_ns, s, count ? 1 : 0);
   if (rc) return cuda_status(rc, "eval_terms");
-  launch_sum_partials(p.red, grid, 2, out, 0, s);
+  if (count) {
+    // (sum, sum^2, count) partials: the count goes to out[8]
+    launch_sum_partials(p.red, grid, 3, p.red + (size_t)grid * 3, 0, s);
+    cudaMemcpyAsync(out, p.red + (size_t)grid * 3, 2 * sizeof(double), cudaMemcpyDeviceToDevice, s);
+    cudaMemcpyAsync(out + 8, p.red + (size_t)grid * 3 + 2, sizeof(double),
+                    cudaMemcpyDeviceToDevice, s);
+  } else {
+    launch_sum_partials(p.red, grid, 2, out, 0, s);
+  }
   const int g2 = sparse_terms_grid(nnz);
   launch_sparse_terms_coo(A, B, Dp, ei, ej, v, nnz, p.sp, g2, s);
   launch_sum_partials(p.sp, g2, 6, out + 2, 0, s);
   return launched("eval_terms");
+}
+
+int sumac_eval_terms(const float* A, const float* B, int64_t m, int64_t n, int d,
+                     const int32_t* ei, const int32_t* ej, const float* v, int64_t nnz,
+                     double* out, int precision, void* ws, size_t ws_bytes, int* dev_err,
+                     sumac_stream_t stream) {
+  return eval_terms_impl(A, B, m, n, d, ei, ej, v, nnz, out, precision, ws, ws_bytes, dev_err,
+                         stream, false);
+}
+
+int sumac_eval_terms_fnnz(const float* A, const float* B, int64_t m, int64_t n, int d,
+                          const int32_t* ei, const int32_t* ej, const float* v, int64_t nnz,
+                          double* out, int precision, void* ws, size_t ws_bytes, int* dev_err,
+                          sumac_stream_t stream) {
+  return eval_terms_impl(A, B, m, n, d, ei, ej, v, nnz, out, precision, ws, ws_bytes, dev_err,
+                         stream, true);
 }
 
 struct LossPlan {

@@ -458,6 +458,170 @@ void launch_salsa_prep(const float* Ffix, const int64_t* rows, int64_t b, int d,
 
 
 // ============================================================================================
+// SALSA block step without the least-squares map P (training/salsa.py:138-140 rewritten):
+// since P = F_I G^{-1}, the product R P equals (R F_I) G^{-1} and the support term
+// sum_i c_ji P_i equals (sum_i c_ji F_i) G^{-1}. So the fused product contracts with C = F_I
+// directly, the finalize pass applies G^{-1} to each row once, and the Gram matrix and its inverse
+// are needed only by the finalize pass: they are computed on a side stream while the product runs.
+//   salsa_gather_kernel  F_I = F[rows] (fp32, tf32 hi / lo halves), C^T = F_I^T (split in 3xTF32
+//                        mode) and the operand maxima of the TF32 product, 32 rows per CTA
+//   salsa_ginv_kernel    partial Gram per 64 rows (fp64); the last CTA sums the partials in a fixed
+//                        order, factors G (warp_lu: LAPACK getrf's pivot choice) and writes
+//                        G^{-1} [Dp][Dp] (fp32, zero outside d x d) column by column
+// ============================================================================================
+__global__ void __launch_bounds__(256) salsa_gather_kernel(
+    const float* __restrict__ Ffix, const int64_t* __restrict__ rows, int64_t b, int Dp,
+    float* __restrict__ FI, float* __restrict__ Fhi, float* __restrict__ Flo,
+    float* __restrict__ Cthi, float* __restrict__ Ctlo, int64_t ldct, unsigned int* stats) {
+  extern __shared__ float tile[];  // [32][Dp + 1]
+  const int64_t r0 = (int64_t)blockIdx.x * 32;
+  const int nr = (int)min((int64_t)32, b - r0);
+  const int ld = Dp + 1;
+  float amax = 0.f;
+  for (int i = threadIdx.x; i < nr * Dp; i += blockDim.x) {
+    const int rr = i / Dp, c = i - rr * Dp;
+    const float v = Ffix[rows[r0 + rr] * Dp + c];
+    tile[rr * ld + c] = v;
+    amax = fmaxf(amax, fabsf(v));
+    const int64_t o = (r0 + rr) * Dp + c;
+    FI[o] = v;
+    if (Fhi) {
+      const float h = tf32_hi(v);
+      Fhi[o] = h;
+      Flo[o] = tf32_lo(v, h);
+    }
+  }
+  __syncthreads();
+  // transposed copy: for column c, the CTA's 32 rows are 32 consecutive floats
+  for (int i = threadIdx.x; i < Dp * 32; i += blockDim.x) {
+    const int c = i >> 5, rr = i & 31;
+    if (rr < nr) {
+      const float v = tile[rr * ld + c];
+      if (Ctlo) {
+        const float h = tf32_hi(v);
+        Cthi[c * ldct + r0 + rr] = h;
+        Ctlo[c * ldct + r0 + rr] = tf32_lo(v, h);
+      } else {
+        Cthi[c * ldct + r0 + rr] = v;
+      }
+    }
+  }
+  if (stats) {
+    float n2 = 0.f;
+    if ((int)threadIdx.x < nr)
+      for (int c = 0; c < Dp; ++c) n2 = fmaf(tile[threadIdx.x * ld + c], tile[threadIdx.x * ld + c], n2);
+    float fm = sqrtf(n2);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      fm = fmaxf(fm, __shfl_xor_sync(0xffffffffu, fm, o));
+      amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    }
+    if ((threadIdx.x & 31) == 0) {
+      atomicMax(&stats[0], __float_as_uint(fm));
+      atomicMax(&stats[1], __float_as_uint(amax));
+    }
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(256) salsa_ginv_kernel(
+    const float* __restrict__ FI, int64_t b, int d, int Dp, double* __restrict__ parts,
+    unsigned int* counter, double* __restrict__ LU, int* __restrict__ piv,
+    float* __restrict__ ginv, int* err) {
+  __shared__ float srow[PREP_ROWS * (D + 1)];
+  __shared__ double sG[D * D];
+  __shared__ bool last;
+  const int64_t r0 = (int64_t)blockIdx.x * PREP_ROWS;
+  const int nr = (int)min((int64_t)PREP_ROWS, b - r0);
+  for (int i = threadIdx.x; i < nr * D; i += blockDim.x) {
+    const int rr = i / D, c = i - rr * D;
+    srow[rr * (D + 1) + c] = c < d ? FI[(r0 + rr) * Dp + c] : 0.f;
+  }
+  __syncthreads();
+  const int dd = d * d;
+  for (int e = threadIdx.x; e < dd; e += blockDim.x) {
+    const int i = e / d, j = e - i * d;
+    double s = 0.0;
+    for (int rr = 0; rr < nr; ++rr)
+      s += (double)srow[rr * (D + 1) + i] * (double)srow[rr * (D + 1) + j];
+    parts[(size_t)blockIdx.x * dd + e] = s;
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  for (int e = threadIdx.x; e < dd; e += blockDim.x) {
+    double s = 0.0;
+#pragma unroll 8
+    for (int q = 0; q < (int)gridDim.x; ++q) s += __ldcg(&parts[(size_t)q * dd + e]);
+    sG[e] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) warp_lu<D>(sG, d, LU, piv, err);
+  __threadfence_block();
+  __syncthreads();
+  // column c of G^{-1}: solve P L U x = e_c (exchanges applied as getrf recorded them)
+  if ((int)threadIdx.x < Dp) {
+    const int c = threadIdx.x;
+    double x[D];
+#pragma unroll
+    for (int k = 0; k < D; ++k) x[k] = (k == c && c < d) ? 1.0 : 0.0;
+#pragma unroll
+    for (int k = 0; k < D; ++k) {
+      const int pk = piv[k];
+#pragma unroll
+      for (int j = k + 1; j < D; ++j)
+        if (j == pk) { const double tv = x[k]; x[k] = x[j]; x[j] = tv; }
+    }
+#pragma unroll
+    for (int i = 1; i < D; ++i) {
+      double s = x[i];
+#pragma unroll
+      for (int j = 0; j < i; ++j) s -= LU[i * D + j] * x[j];
+      x[i] = s;
+    }
+#pragma unroll
+    for (int i = D - 1; i >= 0; --i) {
+      double s = x[i];
+#pragma unroll
+      for (int j = i + 1; j < D; ++j) s -= LU[i * D + j] * x[j];
+      x[i] = s / LU[i * D + i];
+    }
+    for (int k = 0; k < Dp; ++k) ginv[k * Dp + c] = (k < d && c < d) ? (float)x[k] : 0.f;
+  }
+  if (threadIdx.x == 0) *counter = 0u;  // ready for the next launch (graph replays included)
+}
+
+size_t salsa_ginv_scratch_bytes(int64_t b, int d) {
+  return (size_t)salsa_gram_parts(b) * d * d * sizeof(double) + 32 * 32 * sizeof(double) +
+         64 * sizeof(int) + 64;
+}
+
+void launch_salsa_gather(const float* Ffix, const int64_t* rows, int64_t b, int Dp, float* FI,
+                         float* Fhi, float* Flo, float* Cthi, float* Ctlo, int64_t ldct,
+                         unsigned int* stats, cudaStream_t stream) {
+  const size_t smem = (size_t)32 * (Dp + 1) * sizeof(float);
+  count_launch();
+  salsa_gather_kernel<<<cdiv64(b, 32), 256, smem, stream>>>(Ffix, rows, b, Dp, FI, Fhi, Flo, Cthi,
+                                                            Ctlo, ldct, stats);
+}
+
+void launch_salsa_ginv(const float* FI, int64_t b, int d, int Dp, void* scratch,
+                       unsigned int* counter, float* ginv, int* err, cudaStream_t stream) {
+  const int np = salsa_gram_parts(b);
+  double* parts = reinterpret_cast<double*>(scratch);
+  double* LU = parts + (size_t)np * d * d;
+  int* piv = reinterpret_cast<int*>(LU + 32 * 32);
+  count_launch();
+  if (Dp == 16)
+    salsa_ginv_kernel<16><<<np, 256, 0, stream>>>(FI, b, d, Dp, parts, counter, LU, piv, ginv, err);
+  else
+    salsa_ginv_kernel<32><<<np, 256, 0, stream>>>(FI, b, d, Dp, parts, counter, LU, piv, ginv, err);
+}
+
+// ============================================================================================
 // operand maxima for the fp16 second MMA: max row norm of F, max |C|
 // ============================================================================================
 __global__ void operand_stats_kernel(const float* __restrict__ F, int64_t N, int Dp,
@@ -538,7 +702,7 @@ __device__ __forceinline__ float support_coef(int mode, float val, float L) {
   return (mode == FIN_SALSA) ? (val - L + fmaxf(L, 0.f)) : (L - val - fmaxf(L, 0.f));
 }
 
-template <int DP>
+template <int DP, bool GINV>
 // 64 registers (4 CTAs of 256 threads per SM): the pass is latency-bound, warps in flight matter
 __global__ void __launch_bounds__(256, 4) finalize_kernel(FinalizeArgs a) {
   constexpr int G = DP / 4 < 32 ? DP / 4 : 32;  // lanes per row
@@ -552,6 +716,13 @@ __global__ void __launch_bounds__(256, 4) finalize_kernel(FinalizeArgs a) {
   const float mu = a.momentum;
   const float one_m_mu = 1.0f - mu;
   const float ub = (a.mode == FIN_SALSA) ? *a.unbias : 1.f;
+  // GINV: y and the support term were contracted with F_I instead of P = F_I G^{-1}; the row's
+  // (y - cor) is multiplied by G^{-1} (fp32, [DP][DP]) before the update
+  __shared__ __align__(16) float sginv[GINV ? DP * DP : 4];
+  if constexpr (GINV) {
+    for (int i = threadIdx.x; i < DP * DP; i += blockDim.x) sginv[i] = a.ginv[i];
+    __syncthreads();
+  }
   // all lanes of a warp run the same iterations (shuffles below use the full mask)
   for (int64_t base = warp_id * RPW; base < a.M; base += nwarps * RPW) {
     const int64_t j = base + gw;
@@ -680,6 +851,44 @@ __global__ void __launch_bounds__(256, 4) finalize_kernel(FinalizeArgs a) {
         }
       }
     }
+    if constexpr (GINV) {
+      // u = (y - cor) G^{-1}: the row's DP values live in its G lanes (slice k4 of 4 columns in
+      // lane k4 % G, register k4 / G); every lane forms its own output columns
+      float4 t[V], u[V];
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        t[v] = make_float4(y[v].x - cor[v].x, y[v].y - cor[v].y, y[v].z - cor[v].z,
+                           y[v].w - cor[v].w);
+        u[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      const int gbase = lane - gl;
+#pragma unroll
+      for (int k4 = 0; k4 < DP / 4; ++k4) {
+        const int src = gbase + k4 % G;
+        const float4 tk = make_float4(__shfl_sync(0xffffffffu, t[k4 / G].x, src),
+                                      __shfl_sync(0xffffffffu, t[k4 / G].y, src),
+                                      __shfl_sync(0xffffffffu, t[k4 / G].z, src),
+                                      __shfl_sync(0xffffffffu, t[k4 / G].w, src));
+        const float tks[4] = {tk.x, tk.y, tk.z, tk.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float* grow = sginv + (4 * k4 + q) * DP;
+#pragma unroll
+          for (int v = 0; v < V; ++v) {
+            const float4 g4 = reinterpret_cast<const float4*>(grow)[gl + v * G];
+            u[v].x = fmaf(tks[q], g4.x, u[v].x);
+            u[v].y = fmaf(tks[q], g4.y, u[v].y);
+            u[v].z = fmaf(tks[q], g4.z, u[v].z);
+            u[v].w = fmaf(tks[q], g4.w, u[v].w);
+          }
+        }
+      }
+#pragma unroll
+      for (int v = 0; v < V; ++v) {
+        y[v] = u[v];
+        cor[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
     if (!active) continue;
 #pragma unroll
     for (int v = 0; v < V; ++v) {
@@ -729,12 +938,20 @@ void launch_finalize(const FinalizeArgs& a, cudaStream_t stream) {
   const int G = a.Dp / 4 < 32 ? a.Dp / 4 : 32;
   const unsigned grid = grid_cap(a.M * G, threads, 148 * 8);
   count_launch();
+  if (a.ginv) {
+    switch (a.Dp) {
+      case 16: finalize_kernel<16, true><<<grid, threads, 0, stream>>>(a); break;
+      case 32: finalize_kernel<32, true><<<grid, threads, 0, stream>>>(a); break;
+      default: break;
+    }
+    return;
+  }
   switch (a.Dp) {
-    case 16: finalize_kernel<16><<<grid, threads, 0, stream>>>(a); break;
-    case 32: finalize_kernel<32><<<grid, threads, 0, stream>>>(a); break;
-    case 64: finalize_kernel<64><<<grid, threads, 0, stream>>>(a); break;
-    case 128: finalize_kernel<128><<<grid, threads, 0, stream>>>(a); break;
-    case 256: finalize_kernel<256><<<grid, threads, 0, stream>>>(a); break;
+    case 16: finalize_kernel<16, false><<<grid, threads, 0, stream>>>(a); break;
+    case 32: finalize_kernel<32, false><<<grid, threads, 0, stream>>>(a); break;
+    case 64: finalize_kernel<64, false><<<grid, threads, 0, stream>>>(a); break;
+    case 128: finalize_kernel<128, false><<<grid, threads, 0, stream>>>(a); break;
+    case 256: finalize_kernel<256, false><<<grid, threads, 0, stream>>>(a); break;
     default: break;
   }
 }

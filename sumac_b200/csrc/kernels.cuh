@@ -26,9 +26,10 @@ int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float
 void launch_operand_stats(const float* F, int64_t N, int Dp, const float* C, int64_t nC,
                           unsigned int* stats, cudaStream_t stream);
 // Reduce mode: partials[grid][2] (grid <= num_sms) hold per-CTA (sum ReLU, sum ReLU^2).
+// With count = 1 the partials are [grid][3]: (sum, sum^2, number of positive entries).
 int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float* Flo, int64_t N,
                        int Dp, bool x3, double* partials, int* grid_out, int* err, int num_sms,
-                       unsigned long long timeout_ns, cudaStream_t stream);
+                       unsigned long long timeout_ns, cudaStream_t stream, int count = 0);
 int product_split_count(int64_t M, int64_t N, int Dp, bool x3, int num_sms);
 bool product_supported(int Dp, bool x3);
 bool reduce_supported(int Dp, bool x3);
@@ -63,6 +64,17 @@ void launch_salsa_prep(const float* Ffix, const int64_t* rows, int64_t b, int d,
                        void* scratch, unsigned int* counter, unsigned int* stats, int* err,
                        cudaStream_t stream);
 
+// SALSA block step with C = F_I (d <= 32): gather F_I = Ffix[rows] (and its tf32 halves, its
+// transpose C^T = F_I^T split in 3xTF32 mode, and the operand maxima into stats[0..1], zero
+// before) in one launch; then G^{-1} of G = F_I^T F_I into ginv [Dp][Dp] (fp32) in one launch whose
+// last CTA factors G. scratch: salsa_ginv_scratch_bytes(b, d); counter zero before the first use.
+size_t salsa_ginv_scratch_bytes(int64_t b, int d);
+void launch_salsa_gather(const float* Ffix, const int64_t* rows, int64_t b, int Dp, float* FI,
+                         float* Fhi, float* Flo, float* Cthi, float* Ctlo, int64_t ldct,
+                         unsigned int* stats, cudaStream_t stream);
+void launch_salsa_ginv(const float* FI, int64_t b, int d, int Dp, void* scratch,
+                       unsigned int* counter, float* ginv, int* err, cudaStream_t stream);
+
 // out[p] = local[rows[p] - lo] if lo <= rows[p] < hi else 0 (Dp floats per row).
 void launch_gather_owned_rows(const float* local, int64_t lo, int64_t hi, const int64_t* rows,
                               int64_t nrows, int Dp, float* out, cudaStream_t stream);
@@ -89,6 +101,7 @@ struct FinalizeArgs {
   int accumulate;         // FIN_GRAD: out += instead of out =
   float momentum, lrate;  // FIN_SALSA
   const float* unbias;    // FIN_SALSA: device scalar
+  const float* ginv;      // FIN_SALSA, Dp <= 32: [Dp][Dp] G^{-1}; ws and Cm were formed with F_I
 };
 void launch_finalize(const FinalizeArgs& a, cudaStream_t stream);
 

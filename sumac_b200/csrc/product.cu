@@ -205,7 +205,7 @@ __global__ void __launch_bounds__(256, 1)
     relu_simt_kernel(const float* __restrict__ X, int M, const float* __restrict__ Fhi,
                      const float* __restrict__ Flo, int N, const float* __restrict__ Cthi,
                      const float* __restrict__ Ctlo, int64_t ldct, float* __restrict__ Y,
-                     double* __restrict__ partials, int step) {
+                     double* __restrict__ partials, int step, int count) {
   constexpr int RB = 64, CB = 32, LDS = DP + 4;   // rows per block, chunk rows, padded stride
   constexpr int YC = DP / 4;                      // output columns per thread
   extern __shared__ __align__(16) float sm[];
@@ -215,7 +215,7 @@ __global__ void __launch_bounds__(256, 1)
   float* sR = sC + (REDUCE ? 0 : CB * DP);  // [RB][CB + 1]
   const int t = threadIdx.x;
   const int r = t >> 2, q = t & 3;
-  double acc_s = 0.0, acc_s2 = 0.0;
+  double acc_s = 0.0, acc_s2 = 0.0, acc_n = 0.0;
   for (int rb = blockIdx.x; rb * RB < M; rb += gridDim.x) {
     const int row0 = rb * RB;
     __syncthreads();
@@ -262,16 +262,18 @@ __global__ void __launch_bounds__(256, 1)
         }
       }
       if constexpr (REDUCE) {
-        float cs = 0.f, cs2 = 0.f;
+        float cs = 0.f, cs2 = 0.f, cn = 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const bool valid = row0 + r < M && c0 + q * 8 + j < N;
           const float v = valid ? fmaxf(s[j], 0.f) : 0.f;
           cs += v;
           cs2 = fmaf(v, v, cs2);
+          cn += v > 0.f ? 1.f : 0.f;
         }
         acc_s += (double)cs;
         acc_s2 += (double)cs2;
+        acc_n += (double)cn;
       } else {
 #pragma unroll
         for (int j = 0; j < 8; ++j)
@@ -301,20 +303,23 @@ __global__ void __launch_bounds__(256, 1)
     }
   }
   if constexpr (REDUCE) {
-    __shared__ double red[2][8];
+    __shared__ double red[3][8];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
       acc_s += __shfl_xor_sync(0xffffffffu, acc_s, o);
       acc_s2 += __shfl_xor_sync(0xffffffffu, acc_s2, o);
+      acc_n += __shfl_xor_sync(0xffffffffu, acc_n, o);
     }
     __syncthreads();
-    if ((t & 31) == 0) { red[0][t >> 5] = acc_s; red[1][t >> 5] = acc_s2; }
+    if ((t & 31) == 0) { red[0][t >> 5] = acc_s; red[1][t >> 5] = acc_s2; red[2][t >> 5] = acc_n; }
     __syncthreads();
     if (t == 0) {
-      double a = 0.0, b = 0.0;
-      for (int w = 0; w < 8; ++w) { a += red[0][w]; b += red[1][w]; }
-      partials[2 * blockIdx.x] = a;
-      partials[2 * blockIdx.x + 1] = b;
+      double a = 0.0, b = 0.0, c = 0.0;
+      for (int w = 0; w < 8; ++w) { a += red[0][w]; b += red[1][w]; c += red[2][w]; }
+      const int stride = count ? 3 : 2;
+      partials[stride * blockIdx.x] = a;
+      partials[stride * blockIdx.x + 1] = b;
+      if (count) partials[stride * blockIdx.x + 2] = c;
     }
   }
 }
@@ -323,7 +328,7 @@ template <bool REDUCE>
 static int launch_simt(const float* X, int64_t M, const float* Fhi, const float* Flo, int64_t N,
                        const float* Cthi, const float* Ctlo, int64_t ldct, float* Y,
                        double* partials, int num_sms, cudaStream_t stream, int* grid_out,
-                       int step) {
+                       int step, int count = 0) {
   constexpr int DP = 256, LDS = DP + 4;
   constexpr size_t smem = sizeof(float) * (64 * LDS + 32 * LDS + (REDUCE ? 0 : 32 * DP) +
                                            (REDUCE ? 0 : 64 * 33));
@@ -341,7 +346,7 @@ static int launch_simt(const float* X, int64_t M, const float* Fhi, const float*
   if (grid_out) *grid_out = grid;
   count_launch();
   kern<<<grid, 256, smem, stream>>>(X, (int)M, Fhi, Flo ? Flo : Fhi, (int)N, Cthi, Ctlo, ldct, Y,
-                                    partials, step);
+                                    partials, step, count);
   return (int)cudaGetLastError();
 }
 
@@ -374,6 +379,7 @@ int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float
   p.Xg = X;
   p.stats = stats;
   p.step = step;
+  p.count = 0;
   const int64_t items = (int64_t)p.n_groups * p.splits;
   const int grid = (int)(items < num_sms ? items : num_sms);
   return dispatch_product(Dp, c, x3, mx, mfh, mfl, mch, mcl, p, grid, stream);
@@ -381,12 +387,12 @@ int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float
 
 int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float* Flo, int64_t N,
                        int Dp, bool x3, double* partials, int* grid_out, int* err, int num_sms,
-                       unsigned long long timeout_ns, cudaStream_t stream) {
+                       unsigned long long timeout_ns, cudaStream_t stream, int count) {
   ProdCfgRt c = reduce_cfg(Dp, x3);
   if (!c.ok) return -1;
   if (M <= 0 || N <= 0 || M >= INT32_MAX || N >= INT32_MAX) return -5;
   if (c.simt) return launch_simt<true>(X, M, Fhi, Flo, N, nullptr, nullptr, 0, nullptr, partials,
-                                       num_sms, stream, grid_out, 0);
+                                       num_sms, stream, grid_out, 0, count);
   const uint32_t box_k = Dp * 4 <= 128 ? Dp : 32;
   CUtensorMap mx, mfh, mfl;
   const CUtensorMapSwizzle sw = row_swizzle(Dp);
@@ -401,6 +407,7 @@ int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float*
   p.Xg = X;
   p.stats = nullptr;
   p.step = 0;
+  p.count = count;
   p.partials = partials;
   p.err = err;
   p.timeout_ns = timeout_ns;

@@ -87,6 +87,9 @@ struct ProductParams {
   // product mode: 0 = R = ReLU(S); 1 = R = step(S) (1 where S > 0, else 0), the mask term of the
   // gradient of sum ReLU(A B^T) (relu_bat_reduce_jit/custom_op.py:74-82)
   int step;
+  // reduce mode: 1 = also count the positive entries (relu_bat_reduce_jit/kernel_nnz.cu); the
+  // per-CTA partials then hold (sum, sum of squares, count), stride 3
+  int count;
 };
 
 template <int DP, int BN, int STAGES, bool X3, bool REDUCE, int G>
@@ -212,6 +215,23 @@ __device__ __forceinline__ void round_tf32_smem(uint8_t* base, int t) {
   }
 }
 
+// One arrival per warp on an mbarrier whose count is the number of arriving warps (an arrival
+// per thread serialises 256 atomic updates of one shared-memory word on the critical path). The
+// lanes' earlier shared-memory and tcgen05 work is ordered before lane 0's release-arrive by the
+// fences each lane executes before calling this and by __syncwarp.
+__device__ __forceinline__ void warp_arrive(uint64_t* bar, int lane) {
+  __syncwarp();
+  if (lane == 0) mbar_arrive(bar);
+}
+
+// A bounded wait whose outcome is the same in every lane of the warp (the .sync.aligned tcgen05
+// instructions that follow need the whole warp).
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          int* err, int code, uint64_t timeout_ns) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, err, code, timeout_ns);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // fp16x2 of (ReLU(lo), ReLU(hi)), round to nearest; lo in the low half.
 __device__ __forceinline__ uint32_t pack_relu_h2(float lo, float hi) {
   uint32_t r;
@@ -248,7 +268,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
   uint64_t* drain = y_empty + G;            // [N1 + N2] each MMA thread's own MMAs completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + Cfg::N1 + Cfg::N2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  double* red = reinterpret_cast<double*>(smem + Cfg::SMEM_DATA + 768);  // [EPI_WARPS][2]
+  double* red = reinterpret_cast<double*>(smem + Cfg::SMEM_DATA + 768);  // [EPI_WARPS][3]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -258,19 +278,19 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], REDUCE ? Cfg::N1 : Cfg::N2);
-      mbar_init(&c16_ready[s], 32);
+      mbar_init(&c16_ready[s], 1);
     }
     for (int b = 0; b < NBUF; ++b) {
       mbar_init(&s_full[b], 1);
-      mbar_init(&r_ready[b], Cfg::EPI_THREADS);
+      mbar_init(&r_ready[b], Cfg::EPI_WARPS);
       mbar_init(&s_free[b], 1);
     }
     for (int g = 0; g < G; ++g) {
       mbar_init(&x_full[g], 1);
-      mbar_init(&x_ready[g], X3 ? 32 : Cfg::EPI_THREADS);
+      mbar_init(&x_ready[g], X3 ? 1 : Cfg::EPI_WARPS);
       mbar_init(&x_empty[g], Cfg::N1);
       mbar_init(&y_full[g], 1);
-      mbar_init(&y_empty[g], Cfg::EPI_THREADS);
+      mbar_init(&y_empty[g], Cfg::EPI_WARPS);
     }
     for (int i = 0; i < Cfg::N1 + Cfg::N2; ++i) mbar_init(&drain[i], 1);
     *abort_flag = 0;
@@ -296,9 +316,8 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
     // ------------------------------------------------------------------ TMA producer
     // lanes 0..15 fill the stages together: lane 0 waits for the stage to be free and posts the
     // expected bytes, lane j < NLOADS issues copy j of the chunk (copies issued by one thread
-    // complete one after another, copies from different lanes overlap); lane 16 + g loads X slot g
-    const int xslot = lane - 16;
-    const bool x_lane = xslot >= 0 && xslot < G;
+    // complete one after another, copies from different lanes overlap). The X tiles are loaded by
+    // the first epilogue warp, so that they do not queue behind the chunk copies of this warp.
     if (lane < 16) {
       bool ok = true;
       uint32_t gch = 0;     // chunks issued
@@ -339,25 +358,6 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           mbar_drain(&full[g % STAGES], (g / STAGES) & 1);
         }
       }
-    } else if (x_lane) {
-      bool ok = true;
-      uint32_t xuses = 0;   // loads this lane issued into its X slot
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
-        const WorkItem w = work_item(p, item);
-        if (xslot >= w.ntiles) continue;
-        if (xuses > 0 && !mbar_wait(&x_empty[xslot], (xuses - 1) & 1, abort_flag, p.err,
-                                    DEV_TIMEOUT_X, p.timeout_ns)) { ok = false; break; }
-        uint8_t* xdst = sX + xslot * Cfg::XBUF_BYTES;
-        mbar_arrive_expect_tx(&x_full[xslot], Cfg::X_BYTES);
-#pragma unroll
-        for (int s = 0; s < Cfg::KSUB; ++s)
-          tma_load_2d(xdst + s * Cfg::TM * Cfg::XW, &tmX, s * Cfg::BOX_K,
-                      (w.tile0 + xslot) * Cfg::TM, &x_full[xslot]);
-        ++xuses;
-        SB_TR(14, xslot);
-      }
-      // wait (bounded) for this lane's own copies still in flight before leaving
-      if (*abort_flag && xuses > 0) mbar_drain(&x_full[xslot], (xuses - 1) & 1);
     }
   } else if (warp == 1 || warp == Cfg::MMA1B_WARP) {
     // ------------------------------------------------------------------ first MMA (S = X F^T)
@@ -519,7 +519,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
     const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
     uint32_t pair = 0;
     uint32_t slot_par = 0;
-    double acc_s = 0.0, acc_s2 = 0.0;
+    double acc_s = 0.0, acc_s2 = 0.0, acc_n = 0.0;
     bool ok = true;
     // fp16 second MMA: C is scaled by 2^ec (fixed per launch), row j of R by 2^er(j)
     int ec = 0;
@@ -531,17 +531,38 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
       if (cmax > 0.f) frexpf(cmax, &ex);
       ec = 14 - ex;
     }
+    uint32_t xuses = 0;  // warp 2, lane g: loads issued into X slot g
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const WorkItem w = work_item(p, item);
+      if (warp == 2) {
+        // lane g loads the group's tile g into X slot g once the slot's previous group is done
+        bool xok = true;
+        if (lane < w.ntiles) {
+          if (xuses > 0)
+            xok = mbar_wait(&x_empty[lane], (xuses - 1) & 1, abort_flag, p.err, DEV_TIMEOUT_X,
+                            p.timeout_ns);
+          if (xok) {
+            uint8_t* xdst = sX + lane * Cfg::XBUF_BYTES;
+            mbar_arrive_expect_tx(&x_full[lane], Cfg::X_BYTES);
+#pragma unroll
+            for (int s = 0; s < Cfg::KSUB; ++s)
+              tma_load_2d(xdst + s * Cfg::TM * Cfg::XW, &tmX, s * Cfg::BOX_K,
+                          (w.tile0 + lane) * Cfg::TM, &x_full[lane]);
+            ++xuses;
+            SB_TR(14, lane);
+          }
+        }
+        if (!__all_sync(0xffffffffu, xok)) { ok = false; break; }
+      }
       if constexpr (Cfg::ROUND) {
         // round the group's X tiles to tf32 in place before the first MMA reads them
         for (int gi = 0; gi < w.ntiles && ok; ++gi) {
-          if (!mbar_wait(&x_full[gi], (slot_par >> gi) & 1u, abort_flag, p.err, DEV_TIMEOUT_X,
+          if (!warp_wait(&x_full[gi], (slot_par >> gi) & 1u, abort_flag, p.err, DEV_TIMEOUT_X,
                          p.timeout_ns)) { ok = false; break; }
           round_tf32_smem<Cfg::X_BYTES / 16, Cfg::EPI_THREADS>(sX + gi * Cfg::XBUF_BYTES,
                                                                threadIdx.x - 64);
           fence_proxy_async_smem();
-          mbar_arrive(&x_ready[gi]);
+          warp_arrive(&x_ready[gi], lane);
         }
         if (!ok) break;
       }
@@ -571,7 +592,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
       for (int c = w.c0; c < w.c1 && ok; ++c) {
         for (int gi = 0; gi < w.ntiles; ++gi, ++pair) {
           const uint32_t buf = pair % NBUF;
-          if (!mbar_wait(&s_full[buf], (pair / NBUF) & 1, abort_flag, p.err, DEV_TIMEOUT_SFULL,
+          if (!warp_wait(&s_full[buf], (pair / NBUF) & 1, abort_flag, p.err, DEV_TIMEOUT_SFULL,
                          p.timeout_ns)) { ok = false; break; }
           tc_fence_after();
           if (warp == 2 && lane == 0) SB_TR(3, pair);
@@ -587,11 +608,23 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           }
           if constexpr (REDUCE) {
             float cs = 0.f, cs2 = 0.f;
+            if (p.count) {
+              float cn = 0.f;
 #pragma unroll
-            for (int i = 0; i < Cfg::EPI_COLS; ++i) {
-              const float r = fmaxf(v[i], 0.f);
-              cs += r;
-              cs2 = fmaf(r, r, cs2);
+              for (int i = 0; i < Cfg::EPI_COLS; ++i) {
+                const float r = fmaxf(v[i], 0.f);
+                cs += r;
+                cs2 = fmaf(r, r, cs2);
+                cn += v[i] > 0.f ? 1.f : 0.f;
+              }
+              acc_n += (double)cn;
+            } else {
+#pragma unroll
+              for (int i = 0; i < Cfg::EPI_COLS; ++i) {
+                const float r = fmaxf(v[i], 0.f);
+                cs += r;
+                cs2 = fmaf(r, r, cs2);
+              }
             }
             acc_s += (double)cs;
             acc_s2 += (double)cs2;
@@ -647,7 +680,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
             tmem_st_wait();
           }
           tc_fence_before();
-          mbar_arrive(&r_ready[buf]);
+          warp_arrive(&r_ready[buf], lane);
           if (lane == 0 && warp == 2) SB_TR(5, pair);
           if (lane == 0 && warp == 9) SB_TR(6, pair);
         }
@@ -656,7 +689,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
       if constexpr (!REDUCE) {
         const int split = item % p.splits;
         for (int gi = 0; gi < w.ntiles; ++gi) {
-          if (!mbar_wait(&y_full[gi], (slot_par >> gi) & 1u, abort_flag, p.err, DEV_TIMEOUT_Y,
+          if (!warp_wait(&y_full[gi], (slot_par >> gi) & 1u, abort_flag, p.err, DEV_TIMEOUT_Y,
                          p.timeout_ns)) { ok = false; break; }
           tc_fence_after();
           if (warp == 2 && lane == 0) SB_TR(12, gi);
@@ -678,7 +711,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
             }
           }
           tc_fence_before();
-          mbar_arrive(&y_empty[gi]);
+          warp_arrive(&y_empty[gi], lane);
           if (warp == 2 && lane == 0) SB_TR(13, gi);
         }
       }
@@ -689,19 +722,29 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
       for (int o = 16; o > 0; o >>= 1) {
         acc_s += __shfl_xor_sync(0xffffffffu, acc_s, o);
         acc_s2 += __shfl_xor_sync(0xffffffffu, acc_s2, o);
+        acc_n += __shfl_xor_sync(0xffffffffu, acc_n, o);
       }
       if (lane == 0) {
-        red[(warp - 2) * 2 + 0] = acc_s;
-        red[(warp - 2) * 2 + 1] = acc_s2;
+        red[(warp - 2) * 3 + 0] = acc_s;
+        red[(warp - 2) * 3 + 1] = acc_s2;
+        red[(warp - 2) * 3 + 2] = acc_n;
       }
       asm volatile("bar.sync 1, %0;" ::"r"(Cfg::EPI_THREADS) : "memory");
       if (threadIdx.x == 64) {
-        double a = 0.0, b = 0.0;
-        for (int wi = 0; wi < Cfg::EPI_WARPS; ++wi) { a += red[2 * wi]; b += red[2 * wi + 1]; }
-        p.partials[2 * blockIdx.x + 0] = a;
-        p.partials[2 * blockIdx.x + 1] = b;
+        double a = 0.0, b = 0.0, c = 0.0;
+        for (int wi = 0; wi < Cfg::EPI_WARPS; ++wi) {
+          a += red[3 * wi];
+          b += red[3 * wi + 1];
+          c += red[3 * wi + 2];
+        }
+        const int stride = p.count ? 3 : 2;
+        p.partials[stride * blockIdx.x + 0] = a;
+        p.partials[stride * blockIdx.x + 1] = b;
+        if (p.count) p.partials[stride * blockIdx.x + 2] = c;
       }
     }
+    // wait (bounded) for this warp's own X copies still in flight before leaving
+    if (warp == 2 && *abort_flag && lane < G && xuses > 0) mbar_drain(&x_full[lane], (xuses - 1) & 1);
   } else if (Cfg::ROUND && warp == Cfg::CPREP_WARP) {
     if constexpr (Cfg::ROUND) {
     // ------------------------------------------------------------------ chunk prep (TF32 mode)
@@ -721,7 +764,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
       for (int c = w.c0; c < w.c1; ++c, ++gch) {
         const int stage = gch % STAGES;
         const uint32_t round = gch / STAGES;
-        if (!mbar_wait(&full[stage], round & 1, abort_flag, p.err, DEV_TIMEOUT_FULL, p.timeout_ns)) {
+        if (!warp_wait(&full[stage], round & 1, abort_flag, p.err, DEV_TIMEOUT_FULL, p.timeout_ns)) {
           ok = false;
           break;
         }
@@ -769,7 +812,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
         }
         }
         fence_proxy_async_smem();
-        mbar_arrive(&c16_ready[stage]);
+        warp_arrive(&c16_ready[stage], lane);
         if (lane == 0) SB_TR(11, gch);
       }
     }
@@ -781,7 +824,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const WorkItem w = work_item(p, item);
       for (int gi = 0; gi < w.ntiles; ++gi) {
-        if (!mbar_wait(&x_full[gi], (slot_par >> gi) & 1u, abort_flag, p.err, DEV_TIMEOUT_X,
+        if (!warp_wait(&x_full[gi], (slot_par >> gi) & 1u, abort_flag, p.err, DEV_TIMEOUT_X,
                        p.timeout_ns)) { ok = false; break; }
         float4* xs = reinterpret_cast<float4*>(sX + gi * Cfg::XBUF_BYTES);
         float4* xl = reinterpret_cast<float4*>(sX + gi * Cfg::XBUF_BYTES + Cfg::X_BYTES);
@@ -793,7 +836,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
                               tf32_lo(v.w, h.w));
         }
         fence_proxy_async_smem();
-        mbar_arrive(&x_ready[gi]);
+        warp_arrive(&x_ready[gi], lane);
       }
       slot_par ^= (1u << w.ntiles) - 1u;
     }

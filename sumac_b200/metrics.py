@@ -23,7 +23,10 @@ def metrics_from_terms(t) -> tuple[float, float, float]:
 
 
 class Evaluator:
-    """Holds the COO support (int32 indices) of the pruned problem on the device."""
+    """Holds the COO support (int32 indices) of the pruned problem on the device. Each call also
+    counts the positive entries of A B^T in the same pass: ``fnnz`` is the MATLAB
+    implementation's fraction nnz(ReLU(A B^T)) / nnz(S) (matlab/sumac/compute_errors.m:62) of
+    the last call."""
 
     def __init__(self, S_index, S_value, d, precision):
         self.ei = S_index[0].to(torch.int32).contiguous()
@@ -31,8 +34,12 @@ class Evaluator:
         self.v = S_value.to(torch.float32).contiguous()
         self.d = d
         self.precision = precision
-        self.out = torch.zeros(8, dtype=torch.float64, device=S_value.device)
+        self.out = torch.zeros(9, dtype=torch.float64, device=S_value.device)
+        self.fnnz = float("nan")
 
     def __call__(self, Ap, Bp):
-        ops.eval_terms(Ap, Bp, self.d, self.ei, self.ej, self.v, self.out, self.precision)
-        return metrics_from_terms(self.out.cpu().tolist())
+        ops.eval_terms(Ap, Bp, self.d, self.ei, self.ej, self.v, self.out, self.precision,
+                       fnnz=True)
+        t = self.out.cpu().tolist()
+        self.fnnz = t[8] / max(self.v.numel(), 1)
+        return metrics_from_terms(t[:8])

@@ -161,17 +161,18 @@ def gd_block_grad(A, B, d, rows, rowptr_b, ent_b, rowptr_a, ent_a, gA, gB, accum
                                 N.stream_ptr(dev)), "gd_block_grad")
 
 
-def eval_terms(A, B, d, ei, ej, v, out=None, precision=SUMAC_3XTF32):
-    """Eight float64 metric terms (see include/sumac_b200.h) on the device."""
+def eval_terms(A, B, d, ei, ej, v, out=None, precision=SUMAC_3XTF32, fnnz=False):
+    """Eight float64 metric terms (see include/sumac_b200.h) on the device; with fnnz=True a
+    ninth, the number of positive entries of A B^T."""
     L = N.lib()
     dev = A.device
     m, n, nnz = A.shape[0], B.shape[0], v.numel()
     if out is None:
-        out = torch.zeros(8, dtype=torch.float64, device=dev)
+        out = torch.zeros(9 if fnnz else 8, dtype=torch.float64, device=dev)
     ws = _ws(dev, L.sumac_eval_terms_workspace_bytes(m, n, nnz, d, precision), "eval")
-    check(L.sumac_eval_terms(ptr(A), ptr(B), m, n, d, ptr(ei), ptr(ej), ptr(v), nnz, ptr(out),
-                             precision, ptr(ws), ws.numel(), ptr(N.err_word(dev)),
-                             N.stream_ptr(dev)), "eval_terms")
+    fn = L.sumac_eval_terms_fnnz if fnnz else L.sumac_eval_terms
+    check(fn(ptr(A), ptr(B), m, n, d, ptr(ei), ptr(ej), ptr(v), nnz, ptr(out), precision, ptr(ws),
+             ws.numel(), ptr(N.err_word(dev)), N.stream_ptr(dev)), "eval_terms")
     return out
 
 

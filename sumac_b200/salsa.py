@@ -8,6 +8,7 @@ the fused tcgen05 product, and the finalize pass with the sparse correction and 
 """
 from __future__ import annotations
 
+import math
 import time
 
 import numpy as np
@@ -174,6 +175,7 @@ def salsa_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfi
         print(f"[epoch 0/{cfg.max_iterations}]: cost = {errZ:.6f}, rmse = {rmse:.6f}, "
               f"jacc = {jacc:.6f}, time = 0.0000s")
     hist = {"cost": [], "rmse": [], "jacc": [], "time": []}
+    best_cost, best = math.inf, None  # keep_best: the evaluated iterate of lowest cost
     t0 = time.time()
     for it in range(1, cfg.max_iterations + 1):
         perm_r = draw_perm(m, gen_rows, dev)
@@ -187,6 +189,10 @@ def salsa_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfi
             hist["rmse"].append(rmse)
             hist["jacc"].append(jacc)
             hist["time"].append(elapsed)
+            if cfg.report_fnnz:
+                hist.setdefault("fnnz", []).append(evaluator.fnnz)
+            if cfg.keep_best and errZ < best_cost:
+                best_cost, best = errZ, (st.Ap.clone(), st.Bp.clone())
             if cfg.verbose:
                 print(f"[epoch {it}/{cfg.max_iterations}]: cost = {errZ:.6f}, rmse = {rmse:.6f}, "
                       f"jacc = {jacc:.6f}, time = {elapsed:.4f}s")
@@ -194,4 +200,9 @@ def salsa_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfi
     if cfg.verbose:
         print(f"\nTotal elapsed time: {time.time() - t0:.2f} sec")
     A, B = st.factors()
+    if cfg.keep_best:
+        # matlab/sumac/salsa_loop.m:61-79: keep the best evaluated iterate and refactor it
+        if best is not None:
+            A, B = best[0][:, :st.d].contiguous(), best[1][:, :st.d].contiguous()
+        A, B = refactor(A, B)
     return A, B, hist

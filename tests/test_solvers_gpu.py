@@ -140,3 +140,72 @@ def test_c1_gd_matches_reference_run(golden, allow_tf32):
     A, B = align_column_signs(A.cpu().numpy(), B.cpu().numpy(), g["A"])
     assert rel_err(A, g["A"]) < (1e-2 if allow_tf32 else 1e-3)
     assert rel_err(B, g["B"]) < (1e-2 if allow_tf32 else 1e-3)
+
+
+@pytest.mark.parametrize("opt", [OptimizerName.SGD, OptimizerName.ADAMW, OptimizerName.ADAM])
+def test_optimizer_steps_match_torch_optim(opt):
+    """The native optimizer steps against torch.optim as the reference builds it
+    (training/gd.py:20-46): SGD with momentum after clip_grad_norm_([A, B], 1.0); Adam / AdamW
+    with the configured betas and eps and no weight decay. Five steps with fresh gradients, the
+    padded columns left at zero."""
+    from sumac_b200.gd import _Optimizer
+    g = torch.Generator(device="cuda").manual_seed(3)
+    d, Dp = 5, 16
+    cfg = SumacConfig(method=SumacMethod.GD, rank=d, optimizer=opt, learning_rate=0.05,
+                      verbose=False)
+    shapes = [(300, d), (200, d)]
+    ref = [torch.nn.Parameter(torch.randn(s, device="cuda", generator=g)) for s in shapes]
+    ours = [torch.zeros((s[0], Dp), device="cuda") for s in shapes]
+    grads = [torch.zeros((s[0], Dp), device="cuda") for s in shapes]
+    for o, r in zip(ours, ref):
+        o[:, :d] = r.detach()
+    native = _Optimizer(cfg, ours, grads, d)
+    if opt == OptimizerName.SGD:
+        topt = torch.optim.SGD(ref, lr=cfg.learning_rate, momentum=cfg.momentum)
+    elif opt == OptimizerName.ADAMW:
+        topt = torch.optim.AdamW(ref, lr=cfg.learning_rate, weight_decay=0.0,
+                                 betas=cfg.adam_betas, eps=cfg.adam_eps)
+    else:
+        topt = torch.optim.Adam(ref, lr=cfg.learning_rate, betas=cfg.adam_betas,
+                                eps=cfg.adam_eps)
+    for _ in range(5):
+        gs = [0.7 * torch.randn(s, device="cuda", generator=g) for s in shapes]
+        for gr, gg in zip(grads, gs):
+            gr.zero_()
+            gr[:, :d] = gg
+        native.step()
+        for r, gg in zip(ref, gs):
+            r.grad = gg.clone()
+        if opt == OptimizerName.SGD:
+            torch.nn.utils.clip_grad_norm_(ref, max_norm=1.0)
+        topt.step()
+    for o, r in zip(ours, ref):
+        torch.testing.assert_close(o[:, :d], r.detach(), rtol=1e-5, atol=1e-6)
+        assert torch.all(o[:, d:] == 0)
+
+
+def test_salsa_keep_best_returns_refactored_best_iterate(golden):
+    """keep_best (matlab/sumac/salsa_loop.m:61-79): the returned factors are the refactored
+    evaluated iterate of lowest cost: their cost equals the history's minimum, and the refactored
+    factors have orthogonal columns with equal Gram diagonals (A^T A = B^T B = diag(s))."""
+    from sumac_b200.metrics import Evaluator
+    from sumac_b200 import ops
+    g = golden("e2e_salsa")
+    A, B, hist = _run(g, SumacMethod.SALSA, eval_interval=1, keep_best=True)
+    d = int(g["rank"])
+    ev = Evaluator(torch.from_numpy(g["S_index"]).cuda(), torch.from_numpy(g["S_value"]).cuda(),
+                   d, ops.SUMAC_3XTF32)
+    # the pruned problem is the golden one without its empty rows / columns
+    rows = np.unique(g["S_index"][0])
+    cols = np.unique(g["S_index"][1])
+    Ap = ops.pad_factor(A.cuda(), ops.padded_rank(d))
+    Bp = ops.pad_factor(B.cuda(), ops.padded_rank(d))
+    full_A = torch.zeros((int(g["m"]), Ap.shape[1]), device="cuda")
+    full_B = torch.zeros((int(g["n"]), Bp.shape[1]), device="cuda")
+    full_A[torch.from_numpy(rows).cuda()] = Ap[torch.from_numpy(rows).cuda()]
+    full_B[torch.from_numpy(cols).cuda()] = Bp[torch.from_numpy(cols).cuda()]
+    _, _, cost = ev(full_A, full_B)
+    assert abs(cost - min(hist["cost"])) <= 1e-5 * min(hist["cost"])
+    GA, GB = (A.T @ A).cpu().numpy(), (B.T @ B).cpu().numpy()
+    np.testing.assert_allclose(GA, np.diag(np.diag(GA)), atol=1e-4 * np.abs(GA).max())
+    np.testing.assert_allclose(np.diag(GA), np.diag(GB), rtol=1e-4)
