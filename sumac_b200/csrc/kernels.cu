@@ -728,10 +728,13 @@ __global__ void __launch_bounds__(256, 4) finalize_kernel(FinalizeArgs a) {
     const int64_t j = base + gw;
     const bool active = j < a.M;
     const int64_t jr = active ? j : base;
-    float4 y[V], x[V], cor[V];
+    float4 y[V], x[V], cor[V], dxv[V];
 #pragma unroll
     for (int v = 0; v < V; ++v) {
       const int c4 = gl + v * G;
+      // the momentum row is loaded with the others, ahead of the dependent sparse loads
+      dxv[v] = a.mode == FIN_SALSA ? reinterpret_cast<const float4*>(a.dX + jr * DP)[c4]
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
       float4 s = reinterpret_cast<const float4*>(a.ws + jr * DP)[c4];
       for (int q = 1; q < a.splits; ++q) {
         const float4 t = reinterpret_cast<const float4*>(a.ws + ((int64_t)q * a.M + jr) * DP)[c4];
@@ -894,7 +897,7 @@ __global__ void __launch_bounds__(256, 4) finalize_kernel(FinalizeArgs a) {
     for (int v = 0; v < V; ++v) {
       const int c4 = gl + v * G;
       if (a.mode == FIN_SALSA) {
-        const float4 dx = reinterpret_cast<const float4*>(a.dX + j * DP)[c4];
+        const float4 dx = dxv[v];
         float4 nx, ndx;
 #define SB_SALSA_COMPONENT(comp)                                   \
   {                                                                \
@@ -1240,6 +1243,45 @@ __global__ void csr_rowptr_kernel(const int32_t* __restrict__ keys, int64_t nnz,
   if (p == nnz - 1) fill(k + 1, nkeys, (int32_t)nnz);
 }
 
+// The same with four consecutive edges per thread (one 16-byte load of keys) and a grid-stride
+// loop over a grid sized to the GPU, for large nnz (keys must be 16-byte aligned).
+__global__ void __launch_bounds__(256) csr_rowptr4_kernel(const int32_t* __restrict__ keys,
+                                                          int64_t nnz, int64_t nkeys,
+                                                          int32_t* __restrict__ rowptr, int* ntask,
+                                                          int4* tasks, int64_t max_tasks) {
+  auto fill = [&](int64_t lo, int64_t hi, int32_t val) {  // rowptr[lo..hi] = val (inclusive)
+    if (hi < lo) return;
+    if (hi - lo + 1 <= CSR_LONG_GAP) {
+      for (int64_t q = lo; q <= hi; ++q) rowptr[q] = val;
+    } else {
+      const int t = atomicAdd(ntask, 1);
+      if (t < max_tasks) tasks[t] = make_int4((int)lo, (int)hi, val, 0);
+    }
+  };
+  const int64_t nq = (nnz + 3) / 4;
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < nq;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t p0 = 4 * q;
+    int k[4];
+    if (p0 + 3 < nnz) {
+      const int4 v = reinterpret_cast<const int4*>(keys)[q];
+      k[0] = v.x; k[1] = v.y; k[2] = v.z; k[3] = v.w;
+    } else {
+      for (int u = 0; u < 4; ++u) k[u] = p0 + u < nnz ? keys[p0 + u] : 0;
+    }
+    int64_t prev = p0 == 0 ? -1 : keys[p0 - 1];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int64_t p = p0 + u;
+      if (p < nnz) {
+        fill(prev + 1, k[u], (int32_t)p);
+        if (p == nnz - 1) fill((int64_t)k[u] + 1, nkeys, (int32_t)nnz);
+        prev = k[u];
+      }
+    }
+  }
+}
+
 __global__ void csr_fill_tasks_kernel(const int* ntask, const int4* tasks, int64_t max_tasks,
                                       int32_t* __restrict__ rowptr) {
   const int nt = (int)min((int64_t)*ntask, max_tasks);
@@ -1297,8 +1339,12 @@ int launch_block_csr(const int64_t* perm, int64_t m_fixed, int num_blocks, const
   }
   const int64_t nkeys = (int64_t)num_blocks * M;
   count_launch();
-  csr_rowptr_kernel<<<grid_cap(nnz > 0 ? nnz : 1, 256, INT32_MAX), 256, 0, stream>>>(
-      keys, nnz, nkeys, rowptr, ntask, tasks, L.max_tasks);
+  if (nnz >= 4 * 148 * 256)
+    csr_rowptr4_kernel<<<grid_cap((nnz + 3) / 4, 256, 148 * 16), 256, 0, stream>>>(
+        keys, nnz, nkeys, rowptr, ntask, tasks, L.max_tasks);
+  else
+    csr_rowptr_kernel<<<grid_cap(nnz > 0 ? nnz : 1, 256, INT32_MAX), 256, 0, stream>>>(
+        keys, nnz, nkeys, rowptr, ntask, tasks, L.max_tasks);
   count_launch();
   csr_fill_tasks_kernel<<<148 * 2, 256, 0, stream>>>(ntask, tasks, L.max_tasks, rowptr);
   return (int)cudaGetLastError();

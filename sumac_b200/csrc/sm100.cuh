@@ -277,10 +277,6 @@ __host__ __device__ constexpr uint32_t umma_idesc_tf32(int M, int N) {
          | ((uint32_t)(M >> 4) << 24);    // M / 16
 }
 
-__device__ __forceinline__ float tf32_hi(float x) {
-  return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
-}
-
 // Round an fp32 bit pattern to the nearest tf32 value (ties to even), keeping it in fp32 form with
 // the low 13 mantissa bits zero; Inf and NaN pass through (a finite value can round up to Inf).
 __device__ __forceinline__ uint32_t tf32_rne_bits(uint32_t u) {
@@ -289,9 +285,13 @@ __device__ __forceinline__ uint32_t tf32_rne_bits(uint32_t u) {
   return u & 0xffffe000u;
 }
 
-// Low half of the 3xTF32 split x = hi + lo with hi = tf32_hi(x): the remainder x - hi (exact in
-// fp32) rounded to the nearest tf32 value, so that the tensor core, which drops the low 13 bits
-// of an fp32 operand, reads it without a one-sided truncation error.
+// The 3xTF32 split x = hi + lo (+ a remainder below 2^-24 |x|): hi = x rounded to the nearest
+// tf32 value, lo = the exact fp32 remainder x - hi rounded to the nearest tf32 value. Both halves
+// are tf32 values, which the tensor core reads exactly. Rounding (rather than truncating) hi gives
+// lo either sign, so the term the split drops (lo_x lo_f) does not bias products one way.
+__device__ __forceinline__ float tf32_hi(float x) {
+  return __uint_as_float(tf32_rne_bits(__float_as_uint(x)));
+}
 __device__ __forceinline__ float tf32_lo(float x, float hi) {
   return __uint_as_float(tf32_rne_bits(__float_as_uint(x - hi)));
 }

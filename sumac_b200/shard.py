@@ -284,6 +284,23 @@ def virtual_positions(pos: Tensor, m: int, nb: int, rank: int, world: int) -> Te
     return torch.where(own, k * bsub + (t - lo), torch.full_like(pos, -1))
 
 
+def combine_block_grads(gA: Tensor, gB: Tensor, block_rows: list[Tensor], gbuf: Tensor,
+                        group=None) -> None:
+    """Complete the gradients of one GD step whose row blocks were split over the ranks: each
+    rank holds grad A on the rows of its sub-blocks (zero on the other rows of the blocks) and a
+    partial grad B over its sub-blocks' entries. grad B is the sum of the partials (allreduce);
+    the blocks' rows of grad A are disjoint between ranks, so their sum (an allreduce of the
+    gathered rows) is exact. Afterwards every rank holds the whole step's gradients."""
+    dist.all_reduce(gB, group=group)
+    for full in block_rows:
+        b = full.numel()
+        if b == 0:
+            continue
+        torch.index_select(gA, 0, full, out=gbuf[:b])
+        dist.all_reduce(gbuf[:b], group=group)
+        gA.index_copy_(0, full, gbuf[:b])
+
+
 class ShardedGDState:
     """One rank of a GD run whose row blocks are split over the ranks. The factors, their
     gradients and the optimizer state are replicated; each rank computes the gradients of its
@@ -365,15 +382,8 @@ class ShardedGDState:
                 first = False
             if first:
                 ops.fill_zero(gB)
-            dist.all_reduce(gB, group=self.group)
-            for k in batch:  # the block's rows of grad A: disjoint per rank, zero elsewhere
-                full = self.blocks[k][1]
-                b = full.numel()
-                if b == 0:
-                    continue
-                torch.index_select(gA, 0, full, out=self.gbuf[:b])
-                dist.all_reduce(self.gbuf[:b], group=self.group)
-                gA.index_copy_(0, full, self.gbuf[:b])
+            combine_block_grads(gA, gB, [self.blocks[k][1] for k in batch], self.gbuf,
+                                self.group)
             self.opt.step()
         if report:
             dist.all_reduce(self.terms, group=self.group)

@@ -131,3 +131,21 @@ def test_no_cpu_fallback():
     args = valid_inputs()
     with pytest.raises(RuntimeError, match="no CPU implementation"):
         sumac_factorize(**args)
+
+
+def test_init_salsa_factors_matches_reference_on_cpu(golden):
+    """init_salsa_factors (training/salsa.py:36-78) run on the CPU with the seed-0 generator, on
+    C1's data: the same draws and steps as the reference give its initial factors exactly
+    (tests/golden/c1_gd.npz holds the reference's A0/B0)."""
+    import numpy as np
+    import torch
+
+    from bench import make_c1
+    from sumac_b200.salsa import init_salsa_factors
+    g = golden("c1_gd")
+    idx, vals, (m, n) = make_c1()
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    A0, B0 = init_salsa_factors(torch.from_numpy(idx), torch.from_numpy(vals), m, n,
+                                int(g["rank"]), gen)
+    np.testing.assert_allclose(A0.numpy(), g["A0"], rtol=1e-5, atol=1e-6 * np.abs(g["A0"]).max())
+    np.testing.assert_allclose(B0.numpy(), g["B0"], rtol=1e-5, atol=1e-6 * np.abs(g["B0"]).max())

@@ -96,3 +96,67 @@ def test_gd_subblocks_partition_every_position_once():
             lo = torch.tensor([subblock_bounds(m, nb, int(kk), r, world)[0] for kk in k])
             assert torch.equal(vv % bsub, pos[own] - k * bs - lo)
         assert torch.all(owner >= 0)
+
+
+def _gd_worker(rank, world, port, q):
+    """Each rank forms the oracle's gradient of its sub-blocks only (its rows of the block, their
+    entries of S), then combine_block_grads completes the step's gradients; they must equal the
+    oracle's gradient of the whole batch of blocks."""
+    try:
+        import numpy as np
+
+        from oracle import sumac_oracle as orc
+        from sumac_b200.shard import combine_block_grads, subblock_bounds
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        rng = np.random.default_rng(0)
+        m, n, d, nb = 41, 30, 4, 3
+        A = rng.standard_normal((m, d))
+        B = rng.standard_normal((n, d))
+        keys = rng.choice(m * n, 300, replace=False)
+        si, sj, sv = keys // n, keys % n, 0.1 + rng.random(300)
+        perm = rng.permutation(m)
+        bs = (m + nb - 1) // nb
+        batch = [0, 2]
+        gA = torch.zeros((m, d), dtype=torch.float64)
+        gB = torch.zeros((n, d), dtype=torch.float64)
+        gA_ref = np.zeros((m, d))
+        gB_ref = np.zeros((n, d))
+        block_rows = []
+        for k in batch:
+            full = perm[k * bs:min(m, (k + 1) * bs)]
+            block_rows.append(torch.from_numpy(full))
+            lo, hi = subblock_bounds(m, nb, k, rank, world)
+            for rows, acc_a, acc_b in ((full[lo:hi], gA, gB), (full, None, None)):
+                pos = {r: t for t, r in enumerate(rows)}
+                sel = [e for e in range(300) if si[e] in pos]
+                li = [pos[si[e]] for e in sel]
+                _, g_ai, g_b = orc.gd_block_grad(A[rows], B, li, sj[sel], sv[sel])
+                if acc_a is not None:
+                    acc_a[torch.from_numpy(rows)] += torch.from_numpy(g_ai)
+                    acc_b += torch.from_numpy(g_b)
+                else:
+                    gA_ref[rows] += g_ai
+                    gB_ref += g_b
+        combine_block_grads(gA, gB, block_rows, torch.zeros((bs, d), dtype=torch.float64))
+        ok = bool(np.allclose(gA.numpy(), gA_ref, rtol=1e-12, atol=1e-12) and
+                  np.allclose(gB.numpy(), gB_ref, rtol=1e-12, atol=1e-12))
+        dist.destroy_process_group()
+        q.put((rank, ok, None))
+    except Exception as e:  # reported to the parent instead of hanging it
+        q.put((rank, repr(e), None))
+
+
+def test_sharded_gd_gradient_combination_two_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gd_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, ok, _ in results:
+        assert ok is True, (rank, ok)

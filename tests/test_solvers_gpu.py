@@ -123,23 +123,40 @@ def test_c1_init_matches_reference(golden):
 
 @pytest.mark.parametrize("allow_tf32", [False, True])
 def test_c1_gd_matches_reference_run(golden, allow_tf32):
-    """BASELINE config C1 end to end: GD, rank 8, 50 iterations from the default initialisation,
-    seed 0, against the reference's own CPU run. fp32-accurate mode (the reference's default):
-    history within 1e-4 relative; TF32 mode: history within 1e-3 relative (the north star's
-    bound). Factors up to column signs."""
+    """BASELINE config C1 end to end: GD, rank 8, 50 iterations, seed 0, against the reference's
+    own CPU run, from the reference's initial factors (the fixture's A0/B0 are exactly the ones
+    its run started from). fp32-accurate mode (the reference's default): history and factors
+    within 1e-4; TF32 mode: within the north star's 1e-3."""
     g = golden("c1_gd")
     idx, vals, m, n = _c1()
     cfg = SumacConfig(method=SumacMethod.GD, rank=int(g["rank"]), max_iterations=int(g["iters"]),
                       eval_interval=10, seed=0, verbose=False, perm_device="cpu",
                       allow_tf32=allow_tf32)
     A, B, hist = sumac_factorize(S_index=idx.cuda(), S_value=vals.cuda(), shape=(m, n),
-                                 config=cfg)
+                                 A_init=torch.from_numpy(g["A0"]).cuda(),
+                                 B_init=torch.from_numpy(g["B0"]).cuda(), config=cfg)
     tol = 1e-3 if allow_tf32 else 1e-4
     for key in ("cost", "rmse", "jacc"):
         np.testing.assert_allclose(hist[key], g[key], rtol=tol)
-    A, B = align_column_signs(A.cpu().numpy(), B.cpu().numpy(), g["A"])
-    assert rel_err(A, g["A"]) < (1e-2 if allow_tf32 else 1e-3)
-    assert rel_err(B, g["B"]) < (1e-2 if allow_tf32 else 1e-3)
+    assert rel_err(A.cpu().numpy(), g["A"]) < tol
+    assert rel_err(B.cpu().numpy(), g["B"]) < tol
+
+
+def test_c1_gd_from_own_init_close_to_reference_run(golden):
+    """The same run from this library's own initial factors (computed on the GPU). The
+    initialisation has one dominant singular value (~1.5e3) and seven small ones (0.016-0.06):
+    the small columns carry the GPU/CPU rounding difference of the QR/SVD at a relative size far
+    above 1e-5, and Adam, which scales every entry's step alike, carries it on. The history stays
+    within 1e-3 of the reference's (the factors themselves are compared from the reference's
+    initialisation above)."""
+    g = golden("c1_gd")
+    idx, vals, m, n = _c1()
+    cfg = SumacConfig(method=SumacMethod.GD, rank=int(g["rank"]), max_iterations=int(g["iters"]),
+                      eval_interval=10, seed=0, verbose=False, perm_device="cpu")
+    A, B, hist = sumac_factorize(S_index=idx.cuda(), S_value=vals.cuda(), shape=(m, n),
+                                 config=cfg)
+    for key in ("cost", "rmse", "jacc"):
+        np.testing.assert_allclose(hist[key], g[key], rtol=1e-3)
 
 
 @pytest.mark.parametrize("opt", [OptimizerName.SGD, OptimizerName.ADAMW, OptimizerName.ADAM])
@@ -180,7 +197,7 @@ def test_optimizer_steps_match_torch_optim(opt):
             torch.nn.utils.clip_grad_norm_(ref, max_norm=1.0)
         topt.step()
     for o, r in zip(ours, ref):
-        torch.testing.assert_close(o[:, :d], r.detach(), rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(o[:, :d], r.detach())  # float32 defaults
         assert torch.all(o[:, d:] == 0)
 
 
