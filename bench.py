@@ -214,6 +214,13 @@ def measure_tf32_matmul(device):
     return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
 
 
+def tf32_round(t):
+    """fp32 values rounded to the nearest tf32 value (ties to even), as the library packs F."""
+    u = t.contiguous().view(torch.int32)
+    u = (u + 0xFFF + ((u >> 13) & 1)) & -8192
+    return u.view(torch.float32)
+
+
 def dist_info():
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -298,7 +305,7 @@ def run_ours(args):
         Cthi = (Ct.view(torch.int32) & -8192).view(torch.float32)
         Ctlo = Ct - Cthi
     else:
-        Fhi, Flo, Cthi, Ctlo = FI, None, Ct, None
+        Fhi, Flo, Cthi, Ctlo = tf32_round(FI), None, Ct, None
     splits = lib.sumac_relu_product_splits(n_loc, b, Dp, prec)
     part = torch.empty(splits * n_loc * Dp + 16, device=dev)
     err = _native.err_word(dev)
@@ -687,7 +694,7 @@ def run_product_only(args):
     Ct = torch.zeros((Dp, ldct), device=dev)
     Ct[:d, :b] = torch.randn(d, b, device=dev, generator=g)
     hi = lambda t: (t.view(torch.int32) & -8192).view(torch.float32)  # noqa: E731
-    Fhi, Flo = (hi(F), F - hi(F)) if prec == 3 else (F, None)
+    Fhi, Flo = (hi(F), F - hi(F)) if prec == 3 else (tf32_round(F), None)
     Chi, Clo = (hi(Ct), Ct - hi(Ct)) if prec == 3 else (Ct, None)
     lib = _native.lib()
     splits = lib.sumac_relu_product_splits(M, b, Dp, prec)

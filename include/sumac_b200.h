@@ -51,8 +51,8 @@ long long sumac_kernel_launches(void);
  * The fused product alone on prepared operands (the benchmark view of the hot kernel, as the
  * reference's kernel_benchmarks/relu_bat_c_bench.py times relu_bat_c alone):
  * partials[s][M][Dp] = sum over the chunks of split s of ReLU(X F^T) C, with X[M][Dp],
- * F{hi,lo}[N][Dp], Ct{hi,lo}[Dp][ldct] = C^T (tf32 hi / lo split for SUMAC_3XTF32; lo may be NULL
- * for SUMAC_TF32). The number of splits s is sumac_relu_product_splits(M, N, Dp, precision);
+ * F{hi,lo}[N][Dp], Ct{hi,lo}[Dp][ldct] = C^T (tf32 hi / lo split for SUMAC_3XTF32; for SUMAC_TF32
+ * lo may be NULL and Fhi holds F rounded to tf32 values: the kernel rounds X itself). The number of splits s is sumac_relu_product_splits(M, N, Dp, precision);
  * `partials` must hold s*M*Dp floats plus 4 more (scratch for the operand maxima of SUMAC_TF32).
  */
 int sumac_relu_product_splits(int64_t M, int64_t N, int Dp, int precision);

@@ -142,7 +142,7 @@ int sumac_relu_product(const float* X, int64_t M, const float* Fhi, const float*
   }
   int rc = launch_relu_product(X, M, Fhi, Flo, Cthi, Ctlo, ldct, N, Dp, x3, partials, dev_err,
                                num_sms_current(), g_timeout_ns,
-                               reinterpret_cast<cudaStream_t>(stream), stats);
+                               reinterpret_cast<cudaStream_t>(stream), stats, 0, 1);
   return cuda_status(rc, "relu_product");
 }
 int sumac_relu_product_splits(int64_t M, int64_t N, int Dp, int precision) {
@@ -208,13 +208,13 @@ int sumac_relu_bat_c_mode(const float* A, const float* B, const float* C, int64_
   if (!ws || ws_bytes < p.bytes) return fail(SUMAC_ERR_WORKSPACE, "relu_bat_c: workspace %zu < %zu", ws_bytes, p.bytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   launch_gather_pad(B, D, D, nullptr, M, Dp, p.Xp, nullptr, nullptr, s);
-  if (x3) launch_gather_pad(A, D, D, nullptr, N, Dp, nullptr, p.Fp, p.Flo, s);
-  else launch_gather_pad(A, D, D, nullptr, N, Dp, p.Fp, nullptr, nullptr, s);
+  // F as tf32 hi / lo halves (3xTF32) or rounded to tf32 (TF32)
+  launch_gather_pad(A, D, D, nullptr, N, Dp, nullptr, p.Fp, x3 ? p.Flo : nullptr, s);
   launch_gather_pad(C, D, D, nullptr, N, Dp, p.Cp, nullptr, nullptr, s);
   launch_transpose_split(p.Cp, N, Dp, p.Cthi, p.Ctlo, p.ldct, s);
   if (!x3) launch_operand_stats(p.Fp, N, Dp, p.Cthi, (int64_t)Dp * p.ldct, p.stats, s);
   int rc = launch_relu_product(p.Xp, M, p.Fp, p.Flo, p.Cthi, p.Ctlo, p.ldct, N, Dp, x3, p.part,
-                               dev_err, sms, g_timeout_ns, s, p.stats, mode == SUMAC_STEP);
+                               dev_err, sms, g_timeout_ns, s, p.stats, mode == SUMAC_STEP, 1);
   if (rc) return cuda_status(rc, "relu_bat_c");
   FinalizeArgs f{};
   f.mode = FIN_STORE; f.M = M; f.Dp = Dp; f.splits = product_split_count(M, N, Dp, x3, sms);
@@ -260,11 +260,10 @@ int sumac_relu_bat_reduce(const float* A, const float* B, int64_t M, int64_t N, 
   if (!ws || ws_bytes < p.bytes) return fail(SUMAC_ERR_WORKSPACE, "relu_bat_reduce: workspace %zu < %zu", ws_bytes, p.bytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   launch_gather_pad(A, D, D, nullptr, M, Dp, p.Xp, nullptr, nullptr, s);
-  if (x3) launch_gather_pad(B, D, D, nullptr, N, Dp, nullptr, p.Fp, p.Flo, s);
-  else launch_gather_pad(B, D, D, nullptr, N, Dp, p.Fp, nullptr, nullptr, s);
+  launch_gather_pad(B, D, D, nullptr, N, Dp, nullptr, p.Fp, x3 ? p.Flo : nullptr, s);
   int grid = 0;
   int rc = launch_relu_reduce(p.Xp, M, p.Fp, p.Flo, N, Dp, x3, p.part, &grid, dev_err, sms,
-                              g_timeout_ns, s);
+                              g_timeout_ns, s, 0, 1);
   if (rc) return cuda_status(rc, "relu_bat_reduce");
   launch_sum_partials(p.part, grid, 2, out, 0, s);
   return launched("relu_bat_reduce");
@@ -281,7 +280,7 @@ static MpPlan plan_masked(void* ws, int64_t M, int64_t N, int Dp, bool x3, int s
   Bump b(ws);
   MpPlan p;
   p.ldct = round4(N);
-  p.Fhi = x3 ? b.take<float>((size_t)N * Dp) : nullptr;
+  p.Fhi = b.take<float>((size_t)N * Dp);
   p.Flo = x3 ? b.take<float>((size_t)N * Dp) : nullptr;
   p.Cthi = b.take<float>((size_t)Dp * p.ldct);
   p.Ctlo = x3 ? b.take<float>((size_t)Dp * p.ldct) : nullptr;
@@ -312,7 +311,7 @@ int sumac_masked_product(const float* X, const float* F, const float* C, int64_t
   MpPlan p = plan_masked(ws, M, N, Dp, x3, sms);
   if (!ws || ws_bytes < p.bytes) return fail(SUMAC_ERR_WORKSPACE, "masked_product: workspace %zu < %zu", ws_bytes, p.bytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (x3) launch_gather_pad(F, Dp, Dp, nullptr, N, Dp, nullptr, p.Fhi, p.Flo, s);
+  launch_gather_pad(F, Dp, Dp, nullptr, N, Dp, nullptr, p.Fhi, x3 ? p.Flo : nullptr, s);
   launch_transpose_split(C, N, Dp, p.Cthi, p.Ctlo, p.ldct, s);
   if (!x3) launch_operand_stats(F, N, Dp, p.Cthi, (int64_t)Dp * p.ldct, p.stats, s);
   FinalizeArgs f{};
@@ -320,8 +319,8 @@ int sumac_masked_product(const float* X, const float* F, const float* C, int64_t
   f.ws = p.part; f.X = const_cast<float*>(X); f.F = F; f.Cm = C;
   f.rowptr = rowptr; f.ent = reinterpret_cast<const int2*>(ent);
   f.out = Y; f.out_d = Dp; f.ld_out = Dp;
-  int rc = launch_relu_product(X, M, x3 ? p.Fhi : F, p.Flo, p.Cthi, p.Ctlo, p.ldct, N, Dp, x3,
-                               p.part, dev_err, sms, g_timeout_ns, s, p.stats);
+  int rc = launch_relu_product(X, M, p.Fhi, p.Flo, p.Cthi, p.Ctlo, p.ldct, N, Dp, x3,
+                               p.part, dev_err, sms, g_timeout_ns, s, p.stats, 0, 1);
   if (rc) return cuda_status(rc, "masked_product");
   launch_finalize(f, s);
   return launched("masked_product");
@@ -340,14 +339,13 @@ static SalsaPlan plan_salsa(void* ws, int64_t M, int64_t b, int d, int Dp, bool 
   SalsaPlan p;
   p.ldct = round4(b);
   p.FI = bp.take<float>((size_t)b * Dp);
-  p.Fhi = x3 ? bp.take<float>((size_t)b * Dp) : nullptr;
+  p.Fhi = bp.take<float>((size_t)b * Dp);
   p.Flo = x3 ? bp.take<float>((size_t)b * Dp) : nullptr;
   p.P = bp.take<float>((size_t)b * Dp);
   p.Cthi = bp.take<float>((size_t)Dp * p.ldct);
   p.Ctlo = x3 ? bp.take<float>((size_t)Dp * p.ldct) : nullptr;
   const size_t gbytes = (size_t)gram_parts(b) * d * d * sizeof(double);
-  size_t pbytes = salsa_prep_scratch_bytes(b, d);
-  if (d <= 32 && salsa_ginv_scratch_bytes(b, d) > pbytes) pbytes = salsa_ginv_scratch_bytes(b, d);
+  const size_t pbytes = d <= 32 ? salsa_ginv_scratch_bytes(b, d) : 0;
   p.gram = bp.take<double>(((gbytes > pbytes ? gbytes : pbytes) + 7) / 8);
   p.ginv = bp.take<float>((size_t)Dp * Dp);
   p.counter = bp.take<unsigned int>(64);  // [0] done-CTA counter, [1..2] operand maxima
@@ -401,8 +399,8 @@ int sumac_salsa_block_update(const float* F, int64_t m_fixed, const int64_t* row
     cudaStreamWaitEvent(side->stream, side->fork, 0);
     launch_salsa_ginv(p.FI, b, d, Dp, p.gram, p.counter, p.ginv, dev_err, side->stream);
     cudaEventRecord(side->join, side->stream);
-    int rc = launch_relu_product(X, M, x3 ? p.Fhi : p.FI, p.Flo, p.Cthi, p.Ctlo, p.ldct, b, Dp,
-                                 x3, p.part, dev_err, sms, g_timeout_ns, s, p.counter + 1);
+    int rc = launch_relu_product(X, M, p.Fhi, p.Flo, p.Cthi, p.Ctlo, p.ldct, b, Dp,
+                                 x3, p.part, dev_err, sms, g_timeout_ns, s, p.counter + 1, 0, 1);
     cudaStreamWaitEvent(s, side->join, 0);
     if (rc) return cuda_status(rc, "salsa_block_update");
     FinalizeArgs f{};
@@ -413,23 +411,18 @@ int sumac_salsa_block_update(const float* F, int64_t m_fixed, const int64_t* row
     launch_finalize(f, s);
     return launched("salsa_block_update");
   }
-  if (d <= 32) {
-    cudaMemsetAsync(p.counter, 0, 3 * sizeof(unsigned int), s);
-    launch_salsa_prep(F, rows, b, d, Dp, p.FI, p.Fhi, p.Flo, p.P, p.Cthi, p.Ctlo, p.ldct, p.gram,
-                      p.counter, x3 ? nullptr : p.counter + 1, dev_err, s);
-  } else {
-    launch_gather_pad(F, Dp, Dp, rows, b, Dp, p.FI, p.Fhi, p.Flo, s);
-    launch_gram(p.FI, b, d, Dp, p.gram, s);
-    launch_solve(p.FI, b, d, Dp, p.gram, gram_parts(b), p.P, p.Cthi, p.Ctlo, p.ldct, dev_err, s);
-    if (!x3) launch_operand_stats(p.FI, b, Dp, p.Cthi, (int64_t)Dp * p.ldct, p.counter + 1, s);
-  }
+  // d > 32: P = F_I G^{-1} from a block-parallel Gram and a per-row solve, then C = P
+  launch_gather_pad(F, Dp, Dp, rows, b, Dp, p.FI, p.Fhi, x3 ? p.Flo : nullptr, s);
+  launch_gram(p.FI, b, d, Dp, p.gram, s);
+  launch_solve(p.FI, b, d, Dp, p.gram, gram_parts(b), p.P, p.Cthi, p.Ctlo, p.ldct, dev_err, s);
+  if (!x3) launch_operand_stats(p.FI, b, Dp, p.Cthi, (int64_t)Dp * p.ldct, p.counter + 1, s);
   FinalizeArgs f{};
   f.mode = FIN_SALSA; f.M = M; f.Dp = Dp; f.splits = product_split_count(M, b, Dp, x3, sms);
   f.ws = p.part; f.X = X; f.dX = dX; f.F = p.FI; f.Cm = p.P;
   f.rowptr = rowptr; f.ent = reinterpret_cast<const int2*>(ent);
   f.momentum = momentum; f.lrate = lrate; f.unbias = unbias;
-  int rc = launch_relu_product(X, M, x3 ? p.Fhi : p.FI, p.Flo, p.Cthi, p.Ctlo, p.ldct, b, Dp, x3,
-                               p.part, dev_err, sms, g_timeout_ns, s, p.counter + 1);
+  int rc = launch_relu_product(X, M, p.Fhi, p.Flo, p.Cthi, p.Ctlo, p.ldct, b, Dp, x3,
+                               p.part, dev_err, sms, g_timeout_ns, s, p.counter + 1, 0, 1);
   if (rc) return cuda_status(rc, "salsa_block_update");
   launch_finalize(f, s);
   return launched("salsa_block_update");
@@ -470,7 +463,7 @@ static GdPlan plan_gd(void* ws, int64_t n, int64_t b, int Dp, bool x3, int sms) 
   p.ldb = round4(b);
   p.ldn = round4(n);
   p.AI = bp.take<float>((size_t)b * Dp);
-  p.AIhi = x3 ? bp.take<float>((size_t)b * Dp) : nullptr;
+  p.AIhi = bp.take<float>((size_t)b * Dp);
   p.AIlo = x3 ? bp.take<float>((size_t)b * Dp) : nullptr;
   p.AIthi = bp.take<float>((size_t)Dp * p.ldb);
   p.AItlo = x3 ? bp.take<float>((size_t)Dp * p.ldb) : nullptr;
@@ -517,7 +510,7 @@ int sumac_gd_block_grad(const float* A, const float* B, int64_t n, int d, const 
   if (!ws || ws_bytes < p.bytes) return fail(SUMAC_ERR_WORKSPACE, "gd_block_grad: workspace %zu < %zu", ws_bytes, p.bytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   // pass B: rows j of B, contraction over the b block rows; C = A_I
-  launch_gather_pad(A, Dp, Dp, rows, b, Dp, p.AI, p.AIhi, p.AIlo, s);
+  launch_gather_pad(A, Dp, Dp, rows, b, Dp, p.AI, p.AIhi, x3 ? p.AIlo : nullptr, s);
   launch_transpose_split(p.AI, b, Dp, p.AIthi, p.AItlo, p.ldb, s);
   if (!x3) launch_operand_stats(p.AI, b, Dp, p.AIthi, (int64_t)Dp * p.ldb, p.stats, s);
   FinalizeArgs f{};
@@ -525,8 +518,8 @@ int sumac_gd_block_grad(const float* A, const float* B, int64_t n, int d, const 
   f.ws = p.part; f.X = const_cast<float*>(B); f.F = p.AI; f.Cm = p.AI;
   f.rowptr = rowptr_b; f.ent = reinterpret_cast<const int2*>(ent_b);
   f.out = gB; f.scale = 2.f; f.accumulate = accumulate;
-  int rc = launch_relu_product(B, n, x3 ? p.AIhi : p.AI, p.AIlo, p.AIthi, p.AItlo, p.ldb, b, Dp,
-                               x3, p.part, dev_err, sms, g_timeout_ns, s, p.stats);
+  int rc = launch_relu_product(B, n, p.AIhi, p.AIlo, p.AIthi, p.AItlo, p.ldb, b, Dp,
+                               x3, p.part, dev_err, sms, g_timeout_ns, s, p.stats, 0, 1);
   if (rc) return cuda_status(rc, "gd_block_grad (B pass)");
   launch_finalize(f, s);
   // pass A: rows i of A_I, contraction over all n rows of B; C = B
@@ -632,7 +625,7 @@ static LossPlan plan_loss(void* ws, int64_t n, int64_t b, int Dp, bool x3, int s
   Bump bp(ws);
   LossPlan p;
   p.AI = bp.take<float>((size_t)b * Dp);
-  p.AIhi = x3 ? bp.take<float>((size_t)b * Dp) : nullptr;
+  p.AIhi = bp.take<float>((size_t)b * Dp);
   p.AIlo = x3 ? bp.take<float>((size_t)b * Dp) : nullptr;
   p.red = bp.take<double>((size_t)sms * 2);
   p.sp = bp.take<double>((size_t)sparse_terms_grid(n) * 6);
@@ -661,10 +654,10 @@ int sumac_block_loss_terms(const float* A, const float* B, int64_t n, int d, con
   LossPlan p = plan_loss(ws, n, b, Dp, x3, sms);
   if (!ws || ws_bytes < p.bytes) return fail(SUMAC_ERR_WORKSPACE, "block_loss_terms: workspace %zu < %zu", ws_bytes, p.bytes);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  launch_gather_pad(A, Dp, Dp, rows, b, Dp, p.AI, p.AIhi, p.AIlo, s);
+  launch_gather_pad(A, Dp, Dp, rows, b, Dp, p.AI, p.AIhi, x3 ? p.AIlo : nullptr, s);
   int grid = 0;
-  int rc = launch_relu_reduce(B, n, x3 ? p.AIhi : p.AI, p.AIlo, b, Dp, x3, p.red, &grid, dev_err,
-                              sms, g_timeout_ns, s);
+  int rc = launch_relu_reduce(B, n, p.AIhi, p.AIlo, b, Dp, x3, p.red, &grid, dev_err,
+                              sms, g_timeout_ns, s, 0, 1);
   if (rc) return cuda_status(rc, "block_loss_terms");
   launch_sum_partials(p.red, grid, 2, out, accumulate, s);
   const int g2 = sparse_terms_grid(n);

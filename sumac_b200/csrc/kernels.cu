@@ -245,13 +245,7 @@ void launch_solve(const float* FI, int64_t b, int d, int Dp, const double* gram_
 
 
 // ============================================================================================
-// SALSA prep in two launches (training/salsa.py:138-140):
-//  salsa_gram_kernel   64 gathered rows per CTA: writes F_I (fp32, and tf32 hi / lo halves) and
-//                      the CTA's partial Gram matrix (fp64)
-//  salsa_solve_kernel  every CTA sums the partials in a fixed order, one warp factors G with
-//                      partial pivoting (first maximal |pivot| wins, as LAPACK getrf), and each
-//                      thread solves one row in registers: P[r] = G^{-1} F_I[r] (G symmetric, so
-//                      (G^{-1} F_I^T)^T = F_I G^{-1}); P is written row-major and transposed.
+// SALSA least-squares helpers (training/salsa.py:138-140)
 // ============================================================================================
 static constexpr int PREP_ROWS = 64;
 
@@ -310,153 +304,6 @@ __device__ __forceinline__ void warp_lu(const double* __restrict__ G, int d, dou
   }
 }
 
-// 64 gathered rows per CTA: F_I (fp32 and tf32 hi / lo halves) and the CTA's partial Gram
-// (fp64). The last CTA to finish sums the partials in a fixed order and factors G.
-template <int D>
-__global__ void salsa_gram_kernel(const float* __restrict__ Ffix, const int64_t* __restrict__ rows,
-                                  int64_t b, int d, int Dp, float* __restrict__ FI,
-                                  float* __restrict__ Fhi, float* __restrict__ Flo,
-                                  double* __restrict__ parts, unsigned int* counter,
-                                  double* __restrict__ LU, int* __restrict__ piv,
-                                  unsigned int* stats, int* err) {
-  extern __shared__ float srow[];  // [PREP_ROWS][Dp]
-  __shared__ double sG[D * D];
-  __shared__ bool last;
-  const int64_t r0 = (int64_t)blockIdx.x * PREP_ROWS;
-  const int nr = (int)min((int64_t)PREP_ROWS, b - r0);
-  for (int i = threadIdx.x; i < nr * Dp; i += blockDim.x) {
-    const int rr = i / Dp, c = i - rr * Dp;
-    const float v = Ffix[rows[r0 + rr] * Dp + c];
-    srow[i] = v;
-    const int64_t o = (r0 + rr) * Dp + c;
-    FI[o] = v;
-    if (Fhi) {
-      const float h = tf32_hi(v);
-      Fhi[o] = h;
-      Flo[o] = tf32_lo(v, h);
-    }
-  }
-  __syncthreads();
-  if (stats && threadIdx.x < nr) {
-    float n2 = 0.f;
-    for (int c = 0; c < Dp; ++c) n2 = fmaf(srow[threadIdx.x * Dp + c], srow[threadIdx.x * Dp + c], n2);
-    atomicMax(&stats[0], __float_as_uint(sqrtf(n2)));
-  }
-  const int dd = d * d;
-  for (int e = threadIdx.x; e < dd; e += blockDim.x) {
-    const int i = e / d, j = e - i * d;
-    double s = 0.0;
-    for (int rr = 0; rr < nr; ++rr) s += (double)srow[rr * Dp + i] * (double)srow[rr * Dp + j];
-    parts[(size_t)blockIdx.x * dd + e] = s;
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) last = atomicAdd(counter, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  for (int e = threadIdx.x; e < dd; e += blockDim.x) {
-    double s = 0.0;
-#pragma unroll 8
-    for (int q = 0; q < (int)gridDim.x; ++q) s += __ldcg(&parts[(size_t)q * dd + e]);
-    sG[e] = s;
-  }
-  __syncthreads();
-  if (threadIdx.x < 32) warp_lu<D>(sG, d, LU, piv, err);
-  if (threadIdx.x == 0) *counter = 0u;  // ready for the next launch (graph replays included)
-}
-
-// P[r] = G^{-1} F_I[r] from the packed LU factors; one thread per row, in registers.
-template <int D>
-__global__ void __launch_bounds__(128) salsa_solve_kernel(const float* __restrict__ FI, int64_t b,
-                                                          int d, int Dp,
-                                                          const double* __restrict__ LU,
-                                                          const int* __restrict__ piv_g,
-                                                          float* __restrict__ P,
-                                                          float* __restrict__ Cthi,
-                                                          float* __restrict__ Ctlo, int64_t ldct,
-                                                          unsigned int* stats) {
-  __shared__ double sLU[D][D + 1];
-  __shared__ int piv[D];
-  for (int e = threadIdx.x; e < D * D; e += blockDim.x) sLU[e / D][e % D] = LU[e];
-  if (threadIdx.x < D) piv[threadIdx.x] = piv_g[threadIdx.x];
-  __syncthreads();
-  const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (r >= b) return;
-  double x[D];
-#pragma unroll
-  for (int c = 0; c < D; ++c) x[c] = c < d ? (double)FI[r * Dp + c] : 0.0;
-#pragma unroll
-  for (int k = 0; k < D; ++k) {
-    const int pk = piv[k];
-#pragma unroll
-    for (int j = k + 1; j < D; ++j)
-      if (j == pk) { const double tv = x[k]; x[k] = x[j]; x[j] = tv; }
-  }
-#pragma unroll
-  for (int i = 1; i < D; ++i) {
-    double s = x[i];
-#pragma unroll
-    for (int j = 0; j < i; ++j) s -= sLU[i][j] * x[j];
-    x[i] = s;
-  }
-#pragma unroll
-  for (int i = D - 1; i >= 0; --i) {
-    double s = x[i];
-#pragma unroll
-    for (int j = i + 1; j < D; ++j) s -= sLU[i][j] * x[j];
-    x[i] = s / sLU[i][i];
-  }
-  float amax = 0.f;
-#pragma unroll
-  for (int c = 0; c < D; ++c) {
-    const float v = c < d ? (float)x[c] : 0.f;
-    amax = fmaxf(amax, fabsf(v));
-    P[r * Dp + c] = v;
-    if (Ctlo) {
-      const float h = tf32_hi(v);
-      Cthi[c * ldct + r] = h;
-      Ctlo[c * ldct + r] = tf32_lo(v, h);
-    } else {
-      Cthi[c * ldct + r] = v;
-    }
-  }
-  if (stats) atomicMax(&stats[1], __float_as_uint(amax));
-}
-
-size_t salsa_prep_scratch_bytes(int64_t b, int d) {
-  const int D = d <= 16 ? 16 : 32;
-  return (size_t)salsa_gram_parts(b) * d * d * sizeof(double) + D * D * sizeof(double) +
-         64 * sizeof(int) + 64;
-}
-
-void launch_salsa_prep(const float* Ffix, const int64_t* rows, int64_t b, int d, int Dp, float* FI,
-                       float* Fhi, float* Flo, float* P, float* Cthi, float* Ctlo, int64_t ldct,
-                       void* scratch, unsigned int* counter, unsigned int* stats, int* err,
-                       cudaStream_t stream) {
-  const int np = salsa_gram_parts(b);
-  const int D = Dp;
-  double* parts = reinterpret_cast<double*>(scratch);
-  double* LU = parts + (size_t)np * d * d;
-  int* piv = reinterpret_cast<int*>(LU + D * D);
-  const size_t smem = PREP_ROWS * Dp * sizeof(float);
-  const int grid = cdiv64(b, 128);
-  count_launch();
-  count_launch();
-  if (D == 16) {
-    salsa_gram_kernel<16><<<np, 256, smem, stream>>>(Ffix, rows, b, d, Dp, FI, Fhi, Flo, parts,
-                                                     counter, LU, piv, stats, err);
-    salsa_solve_kernel<16><<<grid, 128, 0, stream>>>(FI, b, d, Dp, LU, piv, P, Cthi, Ctlo, ldct,
-                                                     stats);
-  } else {
-    salsa_gram_kernel<32><<<np, 256, smem, stream>>>(Ffix, rows, b, d, Dp, FI, Fhi, Flo, parts,
-                                                     counter, LU, piv, stats, err);
-    salsa_solve_kernel<32><<<grid, 128, 0, stream>>>(FI, b, d, Dp, LU, piv, P, Cthi, Ctlo, ldct,
-                                                     stats);
-  }
-}
-
-
 // ============================================================================================
 // SALSA block step without the least-squares map P (training/salsa.py:138-140 rewritten):
 // since P = F_I G^{-1}, the product R P equals (R F_I) G^{-1} and the support term
@@ -485,10 +332,10 @@ __global__ void __launch_bounds__(256) salsa_gather_kernel(
     amax = fmaxf(amax, fabsf(v));
     const int64_t o = (r0 + rr) * Dp + c;
     FI[o] = v;
-    if (Fhi) {
+    if (Fhi) {  // tf32 hi / lo halves (3xTF32), or the value rounded to tf32 (TF32: no Flo)
       const float h = tf32_hi(v);
       Fhi[o] = h;
-      Flo[o] = tf32_lo(v, h);
+      if (Flo) Flo[o] = tf32_lo(v, h);
     }
   }
   __syncthreads();

@@ -14,12 +14,14 @@ long long launch_count();
 // ---- fused product / reduce (product.cu) ---------------------------------------------------
 // X [M][Dp], F{hi,lo} [N][Dp], Ct{hi,lo} [Dp][ldct] (row-major, 16-byte aligned rows).
 // Writes ws[splits][M][Dp] partial products (splits = product_split_count(...)); step = 1 replaces
-// ReLU(S) by the 0/1 step of S. Returns 0 or a
+// ReLU(S) by the 0/1 step of S. f_rounded = 1 declares that F already holds tf32 values (TF32
+// mode rounds X and, unless declared, every F chunk in shared memory). Returns 0 or a
 // cudaError_t value; -1 for an unsupported (Dp, x3) combination, -5 bad sizes, -6 tensor map.
 int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float* Flo,
                         const float* Cthi, const float* Ctlo, int64_t ldct, int64_t N, int Dp,
                         bool x3, float* ws, int* err, int num_sms, unsigned long long timeout_ns,
-                        cudaStream_t stream, const unsigned int* stats, int step = 0);
+                        cudaStream_t stream, const unsigned int* stats, int step = 0,
+                        int f_rounded = 0);
 // stats[0] = bits of max_r |F[r]| (row norm over Dp), stats[1] = bits of max |C| over nC values
 // (atomicMax on non-negative float bits; the words must be zero beforehand). The TF32 product
 // (fp16 second MMA) reads them to pick exact power-of-two scales.
@@ -29,7 +31,8 @@ void launch_operand_stats(const float* F, int64_t N, int Dp, const float* C, int
 // With count = 1 the partials are [grid][3]: (sum, sum^2, number of positive entries).
 int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float* Flo, int64_t N,
                        int Dp, bool x3, double* partials, int* grid_out, int* err, int num_sms,
-                       unsigned long long timeout_ns, cudaStream_t stream, int count = 0);
+                       unsigned long long timeout_ns, cudaStream_t stream, int count = 0,
+                       int f_rounded = 0);
 int product_split_count(int64_t M, int64_t N, int Dp, bool x3, int num_sms);
 bool product_supported(int Dp, bool x3);
 bool reduce_supported(int Dp, bool x3);
@@ -52,17 +55,7 @@ void launch_gram(const float* FI, int64_t b, int d, int Dp, double* gram_ws, cud
 void launch_solve(const float* FI, int64_t b, int d, int Dp, const double* gram_ws, int nparts,
                   float* P, float* Cthi, float* Ctlo, int64_t ldct, int* err, cudaStream_t stream);
 
-// Gather + Gram + LU + solve for one SALSA block update (d <= 32) in two launches:
-// FI/Fhi/Flo [b][Dp] (Fhi/Flo null in TF32 mode), P [b][Dp], Ct{hi,lo} [Dp][ldct].
-// scratch: salsa_prep_scratch_bytes(b, d); counter: a device word that is zero before the first
-// launch (the kernels leave it zero).
 int salsa_gram_parts(int64_t b);
-size_t salsa_prep_scratch_bytes(int64_t b, int d);
-// Also accumulates the operand maxima of the following product into stats[0..1] (zero before).
-void launch_salsa_prep(const float* Ffix, const int64_t* rows, int64_t b, int d, int Dp, float* FI,
-                       float* Fhi, float* Flo, float* P, float* Cthi, float* Ctlo, int64_t ldct,
-                       void* scratch, unsigned int* counter, unsigned int* stats, int* err,
-                       cudaStream_t stream);
 
 // SALSA block step with C = F_I (d <= 32): gather F_I = Ffix[rows] (and its tf32 halves, its
 // transpose C^T = F_I^T split in 3xTF32 mode, and the operand maxima into stats[0..1], zero

@@ -50,11 +50,12 @@ struct ProdCfgRt {
 // Per (Dp, precision): the TMEM budget is NBUF * BN (x2 for 3xTF32) S columns plus G * Dp Y
 // columns <= 512; shared memory holds G X slots and the stages.
 static ProdCfgRt product_cfg(int Dp, bool x3) {
+  // TMEM: (MS sets of) G Dp Y columns + NBUF S buffers of BN columns within 512 columns
   if (!x3) {
     switch (Dp) {
       case 16: return {128, 4, 8, true};
       case 32: return {128, 3, 4, true};
-      case 64: return {128, 2, 2, true};
+      case 64: return {128, 2, 1, true};
       case 128: return {64, 2, 1, true};
       case 256: return {32, 1, 1, true};  // tf32 second MMA (no room for an fp16 C copy)
     }
@@ -162,7 +163,7 @@ static int dispatch_product(int Dp, const ProdCfgRt& c, bool x3, const CUtensorM
                             cudaStream_t stream) {
   SB_PRODUCT_CASE(16, 128, 4, false, false, 8)
   SB_PRODUCT_CASE(32, 128, 3, false, false, 4)
-  SB_PRODUCT_CASE(64, 128, 2, false, false, 2)
+  SB_PRODUCT_CASE(64, 128, 2, false, false, 1)
   SB_PRODUCT_CASE(128, 64, 2, false, false, 1)
   SB_PRODUCT_CASE(256, 32, 1, false, false, 1)
   SB_PRODUCT_CASE(16, 64, 4, true, false, 8)
@@ -353,7 +354,7 @@ static int launch_simt(const float* X, int64_t M, const float* Fhi, const float*
 int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float* Flo,
                         const float* Cthi, const float* Ctlo, int64_t ldct, int64_t N, int Dp,
                         bool x3, float* ws, int* err, int num_sms, unsigned long long timeout_ns,
-                        cudaStream_t stream, const unsigned int* stats, int step) {
+                        cudaStream_t stream, const unsigned int* stats, int step, int f_rounded) {
   ProdCfgRt c = product_cfg(Dp, x3);
   if (!c.ok) return -1;
   if (M <= 0 || N <= 0 || M >= INT32_MAX || N >= INT32_MAX) return -5;
@@ -380,6 +381,7 @@ int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float
   p.stats = stats;
   p.step = step;
   p.count = 0;
+  p.f_rounded = f_rounded;
   const int64_t items = (int64_t)p.n_groups * p.splits;
   const int grid = (int)(items < num_sms ? items : num_sms);
   return dispatch_product(Dp, c, x3, mx, mfh, mfl, mch, mcl, p, grid, stream);
@@ -387,7 +389,8 @@ int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float
 
 int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float* Flo, int64_t N,
                        int Dp, bool x3, double* partials, int* grid_out, int* err, int num_sms,
-                       unsigned long long timeout_ns, cudaStream_t stream, int count) {
+                       unsigned long long timeout_ns, cudaStream_t stream, int count,
+                       int f_rounded) {
   ProdCfgRt c = reduce_cfg(Dp, x3);
   if (!c.ok) return -1;
   if (M <= 0 || N <= 0 || M >= INT32_MAX || N >= INT32_MAX) return -5;
@@ -408,6 +411,7 @@ int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float*
   p.stats = nullptr;
   p.step = 0;
   p.count = count;
+  p.f_rounded = f_rounded;
   p.partials = partials;
   p.err = err;
   p.timeout_ns = timeout_ns;
@@ -420,13 +424,13 @@ int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float*
 }  // namespace sb
 
 #ifdef SB_TRACE
-// Copy the CTA-0 timeline of the last product / reduce launch (16 x 512 clock64 stamps).
+// Copy the CTA-0 timeline of the last product / reduce launch (24 x 512 clock64 stamps).
 extern "C" int sumac_debug_trace(unsigned long long* host_dst) {
   cudaDeviceSynchronize();
   return (int)cudaMemcpyFromSymbol(host_dst, sb::g_sb_trace, sizeof(sb::g_sb_trace));
 }
 extern "C" int sumac_debug_trace_clear(void) {
-  static unsigned long long zero[16][512];
+  static unsigned long long zero[24][512];
   return (int)cudaMemcpyToSymbol(sb::g_sb_trace, zero, sizeof(zero));
 }
 #endif

@@ -57,7 +57,7 @@ namespace sb {
 // Optional in-kernel timeline (build with -DSB_TRACE): CTA 0 stamps clock64() at each hand-off of
 // the pipeline into g_sb_trace[event][index]; sumac_debug_trace copies it out. Off by default.
 #ifdef SB_TRACE
-__device__ unsigned long long g_sb_trace[16][512];
+__device__ unsigned long long g_sb_trace[24][512];
 #define SB_TR(ev, i)                                                         \
   do {                                                                       \
     if (blockIdx.x == 0 && (unsigned)(i) < 512u) g_sb_trace[ev][i] = clock64(); \
@@ -90,6 +90,9 @@ struct ProductParams {
   // reduce mode: 1 = also count the positive entries (relu_bat_reduce_jit/kernel_nnz.cu); the
   // per-CTA partials then hold (sum, sum of squares, count), stride 3
   int count;
+  // TF32 mode: 1 = the F operand in global memory already holds tf32 values (rounded to nearest
+  // when it was packed), so its chunks are not rounded again in shared memory
+  int f_rounded;
 };
 
 template <int DP, int BN, int STAGES, bool X3, bool REDUCE, int G>
@@ -128,13 +131,21 @@ struct ProductCfg {
   // S buffers in TMEM: as many as the 512 columns hold next to the Y accumulators (3xTF32
   // product mode keeps a lo half per buffer), at most 8. More buffers in flight hide the round
   // trip of a buffer (first MMA -> epilogue -> second MMA -> free), which bounds small ranks.
+  // product mode, MS = 2 (when two sets of Y accumulators fit next to three S buffers): the two
+  // second-MMA issuers each take half of every pair's K range into their own set of Y
+  // accumulators (the epilogue sums the two), which halves the second MMA's share of the S
+  // buffer's round trip; MS = 1: each issuer takes whole pairs, of the tiles gi % 2 == issuer.
+  // Measured at d = 16: 8 resident tiles with MS = 1 beat 4 tiles with MS = 2 (56 vs 64 us); at
+  // d = 64 one tile with MS = 2 beats MS = 1 (80 vs 96 us)
+  static constexpr int MS =
+      (!REDUCE && 2 * G * DP + 3 * ((X3 && !REDUCE) ? 2 : 1) * BN <= 512) ? 2 : 1;
   static constexpr int NBUF_FIT =
-      (512 - (REDUCE ? 0 : G * DP)) / (((X3 && !REDUCE) ? 2 : 1) * BN);
+      (512 - (REDUCE ? 0 : MS * G * DP)) / (((X3 && !REDUCE) ? 2 : 1) * BN);
   static constexpr int NBUF = NBUF_FIT < 8 ? NBUF_FIT : 8;
   static_assert(NBUF >= 2, "at least two S buffers");
   static constexpr int TMEM_S_LO = NBUF * BN;             // lo halves of R (3xTF32)
   static constexpr int TMEM_Y = (X3 ? 2 : 1) * NBUF * BN; // G Y accumulators follow
-  static_assert(REDUCE ? NBUF * BN <= 512 : TMEM_Y + G * DP <= 512, "TMEM budget");
+  static_assert(REDUCE ? NBUF * BN <= 512 : TMEM_Y + MS * G * DP <= 512, "TMEM budget");
   static constexpr uint32_t IDESC1 = umma_idesc_tf32(TM, BN);
   static constexpr uint32_t IDESC2 = umma_idesc_tf32(TM, DP);
   // kind::f16: f32 accumulate, A and B f16, both K-major
@@ -153,29 +164,39 @@ struct ProductCfg {
   // product mode: second-MMA issuers, warp MMA2_WARP + i takes the tiles gi with gi % N2 == i
   static constexpr int MMA2_WARP = 11;
   static constexpr int N2 = 2;
-  // first-MMA issuers: in TF32 reduce mode warp 1 takes the even pairs and warp MMA1B_WARP the
-  // odd ones (measured 15% faster at the reference's reduce shapes); elsewhere warp 1 alone (a
-  // second issuer gave no gain in product mode, and there its s_free waits can meet commits that
-  // arrive out of order; see the phase-lag assertion below)
-  static constexpr int N1 = (REDUCE && !X3) ? 2 : 1;
-  static constexpr int MMA1B_WARP = N1 == 2 ? 10 : 1;
-  // mbarrier parity waits are only sound when the waiter is at most one phase ahead of the
-  // barrier. A second-MMA issuer owns the tiles gi % N2 == me, so two of its consecutive pairs
-  // can lie up to 2 N2 - 1 pairs apart (one owned tile in a group of 2 N2 - 1 tiles); its wait on
-  // r_ready of the later pair then needs the epilogue to have released the pair NBUF earlier,
-  // i.e. NBUF >= 2 N2 - 1. With N1 > 1 first-MMA issuers in product mode, the s_free commits of
-  // different second-MMA issuers can reach a buffer's barrier out of order, so product mode keeps
-  // one first-MMA issuer. In reduce mode the epilogue releases the buffers in pair order and an
-  // issuer's pairs are N1 apart, so N1 <= NBUF suffices.
-  static_assert(REDUCE ? N1 <= NBUF : (N1 == 1 && NBUF >= 2 * N2 - 1), "barrier phase lag");
+  // first-MMA issuers: in TF32 mode with an even number of S buffers, warp 1 issues the even
+  // pairs and warp MMA1B_WARP the odd ones (a thread issues one tcgen05.mma every ~100-200
+  // cycles whatever its size, so two issuers double the rate); elsewhere warp 1 alone
+  static constexpr int N1 = (!X3 && NBUF % 2 == 0 && NBUF >= 4) ? 2 : 1;
+  static constexpr int MMA1B_WARP = N1 == 1 ? 1 : (REDUCE ? 10 : MMA2_WARP + N2);
+  // The S buffers are split between the first-MMA issuers: pair p belongs to issuer p % N1 and,
+  // as that issuer's k-th pair (k = p / N1), to buffer p % N1 + N1 (k % NB1) in its use k / NB1
+  // (pair_slot). Each buffer is then filled by one issuer in order, so its wait for the buffer's
+  // previous use is at most one phase ahead of the barrier: mbarrier parity waits are only sound
+  // then. A buffer is reused every NBUF pairs in the global order. A second-MMA issuer owns the
+  // tiles gi % N2 == me, so two of its consecutive pairs can lie up to 2 N2 - 1 pairs apart (one
+  // owned tile in a group of 2 N2 - 1 tiles); its wait on r_ready of the later pair needs the
+  // epilogue to have released the buffer's previous use, NBUF pairs earlier: NBUF >= 2 N2 - 1.
+  static constexpr int NB1 = NBUF / N1;
+  static_assert(NBUF % N1 == 0, "S buffers split evenly between the first-MMA issuers");
+  static_assert(REDUCE || MS == 2 || NBUF >= 2 * N2 - 1, "barrier phase lag");
+  static_assert(MS == 1 || MS == N2, "one accumulator set per second-MMA issuer");
   static constexpr int THREADS =
-      REDUCE ? 32 * (X3 ? 11 : 12) : 32 * (MMA2_WARP + N2);
+      REDUCE ? 32 * (X3 ? 11 : 12) : 32 * (MMA2_WARP + N2 + (N1 == 2 ? 1 : 0));
   // mbarriers, TMEM slot and abort flag sit below the epilogue's reduction scratch at +768 B
-  static_assert((3 * STAGES + 3 * NBUF + 5 * G + N1 + N2) * 8 + 8 <= 768, "barrier area");
+  static_assert((3 * STAGES + 3 * NBUF + 5 * G + N1 + N2 + 1) * 8 + 8 <= 768, "barrier area");
   static constexpr int EPI_COLS = BN / 2;                 // S columns per epilogue warp
   static_assert(EPI_COLS % 16 == 0, "epilogue column split");
   static constexpr int LDW = EPI_COLS % 32 == 0 ? 32 : 16;  // tcgen05.ld/st width used
 };
+
+// The S buffer of pair `pair` and which use of that buffer it is (see ProductCfg::NB1).
+template <class Cfg>
+__device__ __forceinline__ void pair_slot(uint32_t pair, uint32_t& buf, uint32_t& use) {
+  const uint32_t k = pair / Cfg::N1;
+  buf = pair % Cfg::N1 + Cfg::N1 * (k % Cfg::NB1);
+  use = k / Cfg::NB1;
+}
 
 // One work item: tiles [tile0, tile0 + ntiles) of a group and chunks [c0, c1) of a split.
 struct WorkItem {
@@ -266,7 +287,8 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
   uint64_t* y_full = x_empty + G;           // [G] Y accumulator complete
   uint64_t* y_empty = y_full + G;           // [G] Y accumulator read out
   uint64_t* drain = y_empty + G;            // [N1 + N2] each MMA thread's own MMAs completed
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + Cfg::N1 + Cfg::N2);
+  uint64_t* x_rounded = drain + Cfg::N1 + Cfg::N2;  // all epilogue warps rounded the group's X
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_rounded + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   double* red = reinterpret_cast<double*>(smem + Cfg::SMEM_DATA + 768);  // [EPI_WARPS][3]
 
@@ -283,16 +305,17 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
     for (int b = 0; b < NBUF; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&r_ready[b], Cfg::EPI_WARPS);
-      mbar_init(&s_free[b], 1);
+      mbar_init(&s_free[b], Cfg::MS);
     }
     for (int g = 0; g < G; ++g) {
       mbar_init(&x_full[g], 1);
       mbar_init(&x_ready[g], X3 ? 1 : Cfg::EPI_WARPS);
       mbar_init(&x_empty[g], Cfg::N1);
-      mbar_init(&y_full[g], 1);
+      mbar_init(&y_full[g], Cfg::MS);
       mbar_init(&y_empty[g], Cfg::EPI_WARPS);
     }
     for (int i = 0; i < Cfg::N1 + Cfg::N2; ++i) mbar_init(&drain[i], 1);
+    mbar_init(x_rounded, Cfg::EPI_WARPS);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -381,16 +404,18 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
         for (int ci = 0; ci < w.c1 - w.c0 && ok; ++ci, ++chunk) {
           const int c = chunk_at(w, ci);
           const int stage = chunk % STAGES;
-          if (!mbar_wait(Cfg::ROUND ? &c16_ready[stage] : &full[stage], (chunk / STAGES) & 1,
+          const bool prepped = Cfg::ROUND && (!REDUCE || !p.f_rounded);
+          if (!mbar_wait(prepped ? &c16_ready[stage] : &full[stage], (chunk / STAGES) & 1,
                          abort_flag, p.err, DEV_TIMEOUT_FULL, p.timeout_ns)) { ok = false; break; }
           const uint32_t fbase = sSt_addr + stage * Cfg::STAGE_ALLOC;
           for (int gi = 0; gi < w.ntiles; ++gi, ++pair) {
             if ((int)(pair % Cfg::N1) != me1) continue;
-            const uint32_t buf = pair % NBUF;
+            uint32_t buf, use;
+            pair_slot<Cfg>(pair, buf, use);
             // the S buffer is free once the epilogue (reduce) or the second MMA (product) is
             // done with its previous use
-            if (pair >= (uint32_t)NBUF &&
-                !mbar_wait(REDUCE ? &r_ready[buf] : &s_free[buf], ((pair / NBUF) - 1) & 1,
+            if (use > 0 &&
+                !mbar_wait(REDUCE ? &r_ready[buf] : &s_free[buf], (use - 1) & 1,
                            abort_flag, p.err, DEV_TIMEOUT_RREADY, p.timeout_ns)) {
               ok = false;
               break;
@@ -453,10 +478,11 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           if (!mbar_wait(Cfg::ROUND ? &c16_ready[stage] : &full[stage], (chunk / STAGES) & 1,
                          abort_flag, p.err, DEV_TIMEOUT_FULL, p.timeout_ns)) { ok = false; break; }
           for (int gi = 0; gi < w.ntiles; ++gi, ++pair) {
-            if (gi % Cfg::N2 != me) continue;
-            const uint32_t buf = pair % NBUF;
+            if (Cfg::MS == 1 && gi % Cfg::N2 != me) continue;
+            uint32_t buf, use;
+            pair_slot<Cfg>(pair, buf, use);
             const bool first = ci == 0;
-            if (!mbar_wait(&r_ready[buf], (pair / NBUF) & 1, abort_flag, p.err, DEV_TIMEOUT_RREADY,
+            if (!mbar_wait(&r_ready[buf], use & 1, abort_flag, p.err, DEV_TIMEOUT_RREADY,
                            p.timeout_ns)) { ok = false; break; }
             if (first && ((slot_used >> gi) & 1u) &&
                 !mbar_wait(&y_empty[gi], ((slot_par >> gi) & 1u) ^ 1u, abort_flag, p.err,
@@ -464,27 +490,32 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
             tc_fence_after();
             SB_TR(7 + 2 * me, pair);
             const uint32_t s_hi = tbase + buf * BN;
-            const uint32_t ytm = tbase + Cfg::TMEM_Y + gi * DP;
+            // this issuer's accumulator set (MS = 2) and its share of the K steps
+            const uint32_t ytm = tbase + Cfg::TMEM_Y + (Cfg::MS == 2 ? me : 0) * G * DP + gi * DP;
             if constexpr (Cfg::H16) {
               // R packed as fp16 pairs: warp half h holds k in [h*EPI_COLS, (h+1)*EPI_COLS) in
               // its own first EPI_COLS/2 columns; C in fp16, 64-element 128 B swizzled sub-tiles
               const uint32_t c16 = stg + Cfg::STAGE_BYTES;
+              constexpr int KK = BN / 16, K0 = Cfg::MS == 2 ? KK / 2 : KK;
 #pragma unroll
-              for (int kk = 0; kk < BN / 16; ++kk) {
+              for (int k = 0; k < K0; ++k) {
+                const int kk = (Cfg::MS == 2 ? me * K0 : 0) + k;
                 const int hh = (16 * kk) / Cfg::EPI_COLS;
                 const uint32_t acol = hh * Cfg::EPI_COLS + (16 * kk - hh * Cfg::EPI_COLS) / 2;
                 const uint32_t off = (kk >> 2) * (DP * 128) + (kk & 3) * 32;
                 const uint64_t bd = umma_sdesc(c16 + off, 16, 1024, UMMA_SW128);
-                mma_f16_ts(ytm, s_hi + acol, bd, Cfg::IDESC2_F16, (first && kk == 0) ? 0u : 1u);
+                mma_f16_ts(ytm, s_hi + acol, bd, Cfg::IDESC2_F16, (first && k == 0) ? 0u : 1u);
               }
             } else {
               const uint32_t s_lo = tbase + Cfg::TMEM_S_LO + buf * BN;
               const uint32_t cbase = stg + Cfg::NPREC * Cfg::F_BYTES;
+              constexpr int KK = BN / 8, K0 = Cfg::MS == 2 ? KK / 2 : KK;
 #pragma unroll
-              for (int kk = 0; kk < BN / 8; ++kk) {
+              for (int k = 0; k < K0; ++k) {
+                const int kk = (Cfg::MS == 2 ? me * K0 : 0) + k;
                 const uint32_t off = (kk >> 2) * (DP * 128) + (kk & 3) * 32;
                 const uint64_t bhi = umma_sdesc(cbase + off, 16, 1024, UMMA_SW128);
-                const uint32_t acc0 = (first && kk == 0) ? 0u : 1u;
+                const uint32_t acc0 = (first && k == 0) ? 0u : 1u;
                 if (X3) {
                   const uint64_t blo = umma_sdesc(cbase + Cfg::C_BYTES + off, 16, 1024, UMMA_SW128);
                   mma_tf32_ts(ytm, s_lo + kk * 8, bhi, Cfg::IDESC2, acc0);
@@ -521,17 +552,13 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
     uint32_t slot_par = 0;
     double acc_s = 0.0, acc_s2 = 0.0, acc_n = 0.0;
     bool ok = true;
-    // fp16 second MMA: C is scaled by 2^ec (fixed per launch), row j of R by 2^er(j)
+    // fp16 second MMA: C is scaled by 2^ec (fixed per launch), row j of R by 2^er(j); read
+    // after the first X tiles are requested (a cold global load)
     int ec = 0;
     float fmax = 0.f;
-    if constexpr (Cfg::H16) {
-      fmax = __uint_as_float(p.stats[0]);
-      const float cmax = __uint_as_float(p.stats[1]);
-      int ex = 0;
-      if (cmax > 0.f) frexpf(cmax, &ex);
-      ec = 14 - ex;
-    }
+    bool stats_read = false;
     uint32_t xuses = 0;  // warp 2, lane g: loads issued into X slot g
+    uint32_t items_done = 0;  // groups this CTA finished (phase of x_rounded)
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const WorkItem w = work_item(p, item);
       if (warp == 2) {
@@ -554,7 +581,65 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
         }
         if (!__all_sync(0xffffffffu, xok)) { ok = false; break; }
       }
-      if constexpr (Cfg::ROUND) {
+      int er[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) er[g] = 0;
+      if constexpr (Cfg::H16) {
+        // TF32 product: row j of X is scaled by 2^er(j) and rounded to tf32 in place, so that S
+        // and R come out scaled (|S_ji| <= |x_j| max_i |F_i| < 2^15 after scaling, inside the
+        // fp16 range of R) and the per-pair epilogue only converts. The exponent comes from the
+        // row's norm, read by both threads that own the row before either rewrites its half.
+        if (!stats_read) {
+          fmax = __uint_as_float(p.stats[0]);
+          const float cmax = __uint_as_float(p.stats[1]);
+          int ex = 0;
+          if (cmax > 0.f) frexpf(cmax, &ex);
+          ec = 14 - ex;
+          stats_read = true;
+        }
+        for (int g = 0; g < w.ntiles && ok; ++g) {
+          if (!warp_wait(&x_full[g], (slot_par >> g) & 1u, abort_flag, p.err, DEV_TIMEOUT_X,
+                         p.timeout_ns)) { ok = false; break; }
+          float n2 = 0.f;
+#pragma unroll
+          for (int sub = 0; sub < Cfg::KSUB; ++sub) {
+            const float4* xr = reinterpret_cast<const float4*>(
+                sX + g * Cfg::XBUF_BYTES + sub * Cfg::TM * Cfg::XW + row_in_tile * Cfg::XW);
+#pragma unroll
+            for (int c = 0; c < Cfg::XW / 16; ++c) {
+              const float4 xv = xr[c];
+              n2 = fmaf(xv.x, xv.x, fmaf(xv.y, xv.y, fmaf(xv.z, xv.z, fmaf(xv.w, xv.w, n2))));
+            }
+          }
+          const float bound = sqrtf(n2) * fmax * 1.001f;
+          int ex = 0;
+          if (bound > 0.f) frexpf(bound, &ex);
+          er[g] = p.step ? 0 : 14 - ex;  // step values are 0 or 1: no scale needed
+        }
+        if (!ok) break;
+        // every epilogue warp has read its rows before any of them is rewritten
+        warp_arrive(x_rounded, lane);
+        if (!warp_wait(x_rounded, items_done & 1u, abort_flag, p.err, DEV_TIMEOUT_X,
+                       p.timeout_ns)) { ok = false; break; }
+        constexpr int UPR = Cfg::KSUB * Cfg::XW / 16;  // 16-byte units per row
+        for (int g = 0; g < w.ntiles; ++g) {
+          const float sc = __int_as_float((127 + er[g]) << 23);
+#pragma unroll
+          for (int u = half * (UPR / 2); u < (half + 1) * (UPR / 2); ++u) {
+            uint4* q = reinterpret_cast<uint4*>(sX + g * Cfg::XBUF_BYTES +
+                                                (u / (Cfg::XW / 16)) * Cfg::TM * Cfg::XW +
+                                                row_in_tile * Cfg::XW) + u % (Cfg::XW / 16);
+            uint4 v = *q;
+            v.x = tf32_rne_bits(__float_as_uint(__uint_as_float(v.x) * sc));
+            v.y = tf32_rne_bits(__float_as_uint(__uint_as_float(v.y) * sc));
+            v.z = tf32_rne_bits(__float_as_uint(__uint_as_float(v.z) * sc));
+            v.w = tf32_rne_bits(__float_as_uint(__uint_as_float(v.w) * sc));
+            *q = v;
+          }
+        }
+        fence_proxy_async_smem();
+        for (int g = 0; g < w.ntiles; ++g) warp_arrive(&x_ready[g], lane);
+      } else if constexpr (Cfg::ROUND) {
         // round the group's X tiles to tf32 in place before the first MMA reads them
         for (int gi = 0; gi < w.ntiles && ok; ++gi) {
           if (!warp_wait(&x_full[gi], (slot_par >> gi) & 1u, abort_flag, p.err, DEV_TIMEOUT_X,
@@ -566,33 +651,11 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
         }
         if (!ok) break;
       }
-      int er[G];
-#pragma unroll
-      for (int g = 0; g < G; ++g) er[g] = 0;
-      if constexpr (Cfg::H16) {
-        // |S_ji| <= |x_j| max_i |F_i|: scale the row so that |R| < 2^15
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const int row = (w.tile0 + g) * Cfg::TM + row_in_tile;
-          if (g < w.ntiles && row < p.M) {
-            const float4* xr = reinterpret_cast<const float4*>(p.Xg + (size_t)row * DP);
-            float n2 = 0.f;
-#pragma unroll
-            for (int c = 0; c < DP / 4; ++c) {
-              const float4 xv = xr[c];
-              n2 = fmaf(xv.x, xv.x, fmaf(xv.y, xv.y, fmaf(xv.z, xv.z, fmaf(xv.w, xv.w, n2))));
-            }
-            const float bound = sqrtf(n2) * fmax * 1.001f;
-            int ex = 0;
-            if (bound > 0.f) frexpf(bound, &ex);
-            er[g] = p.step ? 0 : 14 - ex;  // step values are 0 or 1: no scale needed
-          }
-        }
-      }
       for (int c = w.c0; c < w.c1 && ok; ++c) {
         for (int gi = 0; gi < w.ntiles; ++gi, ++pair) {
-          const uint32_t buf = pair % NBUF;
-          if (!warp_wait(&s_full[buf], (pair / NBUF) & 1, abort_flag, p.err, DEV_TIMEOUT_SFULL,
+          uint32_t buf, use;
+          pair_slot<Cfg>(pair, buf, use);
+          if (!warp_wait(&s_full[buf], use & 1, abort_flag, p.err, DEV_TIMEOUT_SFULL,
                          p.timeout_ns)) { ok = false; break; }
           tc_fence_after();
           if (warp == 2 && lane == 0) SB_TR(3, pair);
@@ -664,7 +727,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           } else {
             // pack ReLU(R) (scaled) as fp16 pairs (even k in the low half) into this warp's own
             // first EPI_COLS / 2 columns
-            const float rscale = __int_as_float((127 + er[gi]) << 23);
+            // S is already scaled by 2^er (X was scaled in shared memory)
             uint32_t pk[Cfg::EPI_COLS / 2];
             if (p.step) {
 #pragma unroll
@@ -673,7 +736,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
             } else {
 #pragma unroll
               for (int i = 0; i < Cfg::EPI_COLS / 2; ++i)
-                pk[i] = pack_relu_h2(v[2 * i] * rscale, v[2 * i + 1] * rscale);
+                pk[i] = pack_relu_h2(v[2 * i], v[2 * i + 1]);
             }
             if constexpr (Cfg::EPI_COLS / 2 == 32) tmem_st32(s_tm, reinterpret_cast<const float*>(pk));
             else tmem_st16(s_tm, reinterpret_cast<const float*>(pk));
@@ -683,6 +746,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           warp_arrive(&r_ready[buf], lane);
           if (lane == 0 && warp == 2) SB_TR(5, pair);
           if (lane == 0 && warp == 9) SB_TR(6, pair);
+          if (lane == 0) SB_TR(16 + warp - 2, pair);
         }
       }
       if (!ok) break;
@@ -702,6 +766,13 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
             float y[16];
             tmem_ld16(tbase + lane_addr + Cfg::TMEM_Y + gi * DP + col, y);
             tmem_ld_wait_regs16(y);
+            if constexpr (Cfg::MS == 2) {
+              float y2[16];
+              tmem_ld16(tbase + lane_addr + Cfg::TMEM_Y + (G + gi) * DP + col, y2);
+              tmem_ld_wait_regs16(y2);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) y[i] += y2[i];
+            }
             if (row < p.M) {
               float4* o4 = reinterpret_cast<float4*>(out + col);
 #pragma unroll
@@ -716,6 +787,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
         }
       }
       slot_par ^= (1u << w.ntiles) - 1u;
+      ++items_done;
     }
     if constexpr (REDUCE) {
 #pragma unroll
@@ -751,6 +823,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
     // rounds the F chunk to tf32 in place; product mode: fp32 C chunk (32-float SW128 sub-tiles)
     // -> fp16 scaled by 2^ec (64-element SW128 sub-tiles), or (Dp = 256) C rounded in place
     float cscale = 1.f;
+    const bool idle = REDUCE && p.f_rounded;  // nothing to prepare: the MMA waits the TMA
     if constexpr (Cfg::H16) {
       const float cmax = __uint_as_float(p.stats[1]);
       int ex = 0;
@@ -758,7 +831,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
       cscale = ldexpf(1.f, 14 - ex);
     }
     uint32_t gch = 0;
-    bool ok = true;
+    bool ok = !idle;
     for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
       const WorkItem w = work_item(p, item);
       for (int c = w.c0; c < w.c1; ++c, ++gch) {
@@ -769,7 +842,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           break;
         }
         uint8_t* stg = sStage + stage * Cfg::STAGE_ALLOC;
-        round_tf32_smem<Cfg::F_BYTES / 16, 32>(stg, lane);
+        if (!p.f_rounded) round_tf32_smem<Cfg::F_BYTES / 16, 32>(stg, lane);
         if constexpr (!REDUCE && !Cfg::H16) round_tf32_smem<Cfg::C_BYTES / 16, 32>(stg + Cfg::F_BYTES, lane);
         if constexpr (Cfg::H16) {
         const uint8_t* src = stg + Cfg::F_BYTES;

@@ -76,6 +76,38 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Bounded wait by polling mbarrier.test_wait (never suspends): for the single-thread MMA issuers,
+// whose wake-up after a suspending try_wait showed a latency of several hundred cycles on the
+// pipeline's critical path. The clock is read every 256 polls.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity,
+                                               volatile int* abort_flag, int* err, int code,
+                                               uint64_t timeout_ns) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        *abort_flag = 1;
+        if (err) atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
 // Bounded wait that ignores the abort flag (used only while draining after an abort).
 __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
   const uint64_t t0 = globaltimer_ns();
