@@ -723,6 +723,31 @@ def run_product_only(args):
                       "ms_per_launch": ms, "tflops": tflops, "max_rel_err_vs_torch": err_rel}))
 
 
+def run_profile_iteration(args):
+    """One eager SALSA iteration at the workload's shapes (both CSR rebuilds and 2 x num_blocks
+    block updates as separate launches, no CUDA graph), after the setup: a short, self-contained
+    command for kernel profiles of the iteration's kernels."""
+    from sumac_b200 import SumacConfig, SumacMethod, _native
+    from sumac_b200.data import prune_zero_rows_cols
+    from sumac_b200.salsa import SalsaState, draw_perm, init_salsa_factors
+    dev = torch.device("cuda", 0)
+    cfgd = CONFIGS[args.config]
+    idx_np, val_np, shape = MAKERS[args.config]()
+    S_index = torch.from_numpy(idx_np).to(dev)
+    S_value = torch.from_numpy(val_np).to(dev)
+    S_index, _, _, m, n = prune_zero_rows_cols(S_index, shape)
+    cfg = SumacConfig(method=SumacMethod.SALSA, rank=cfgd["rank"], num_blocks=cfgd["num_blocks"],
+                      seed=0, verbose=False, allow_tf32=args.precision == "tf32", device=dev)
+    gen, gen_rows, gen_cols = cfg.get_generator()
+    A, B = init_salsa_factors(S_index, S_value, m, n, cfg.rank, gen)
+    st = SalsaState(S_index, S_value, m, n, cfg, A, B)
+    st.use_graph = False
+    st.iteration(1, draw_perm(m, gen_rows, dev), draw_perm(n, gen_cols, dev))
+    torch.cuda.synchronize()
+    _native.raise_device_error(dev)
+    print(json.dumps({"profile_iteration": args.config, "m": m, "n": n}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -735,10 +760,14 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--product-only", action="store_true",
                     help="time the fused product alone at one block update's shapes")
+    ap.add_argument("--profile-iteration", action="store_true",
+                    help="run one eager SALSA iteration (for kernel profiles) and exit")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.product_only:
+    if args.profile_iteration:
+        run_profile_iteration(args)
+    elif args.product_only:
         run_product_only(args)
     elif args.impl == "ours" and CONFIGS[args.config].get("method") == "GD":
         run_gd(args)
