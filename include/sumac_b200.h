@@ -205,6 +205,23 @@ int sumac_sgd_step(float* p, float* g, float* buf, int64_t n, float lr, float mo
 int sumac_fill_zero(float* p, int64_t n, sumac_stream_t stream);
 
 /*
+ * Initial SALSA factors (replaces the sparse products and the gathered dot products of
+ * init_salsa_factors, src/sumac/training/salsa.py:36-78).
+ * sumac_init_factor: out[r][c] = sign * sqrt(sum_{e in [rowptr[r], rowptr[r+1])} val[e] R[col[e]][c])
+ * for r < M, c < d (R and out row-major with d columns): sqrt(S R_A) and -sqrt(S^T R_B) from the
+ * edges sorted by row, summed in edge order.
+ * sumac_init_scale_terms: out[0..2] = (sum v^2, sum v L, sum L^2) in float64 over the nnz entries,
+ * L = <A[ei], B[ej]> in float32 (A, B row-major, d columns); ws of
+ * sumac_init_scale_workspace_bytes() bytes. Both enqueue on `stream`.
+ */
+int sumac_init_factor(const int32_t* rowptr, const int32_t* col, const float* val, int64_t M,
+                      const float* R, int d, float sign, float* out, sumac_stream_t stream);
+size_t sumac_init_scale_workspace_bytes(void);
+int sumac_init_scale_terms(const float* A, const float* B, int d, const int32_t* ei,
+                           const int32_t* ej, const float* v, int64_t nnz, double* out, void* ws,
+                           size_t ws_bytes, sumac_stream_t stream);
+
+/*
  * Row-sharded factors (multi-GPU SALSA): out[p] = local[rows[p] - lo] (Dp floats) when this rank
  * owns global row rows[p] (lo <= rows[p] < hi), zero otherwise. An allreduce(sum) of `out` over the
  * ranks then yields the block rows F[rows] exactly. No counterpart kernel in the reference, whose

@@ -63,6 +63,9 @@ _SIGS = {
     "sumac_grad_sumsq": (i32, [p, i64, p, p]),
     "sumac_sgd_step": (i32, [p, p, p, i64, f32, f32, i32, p, f32, p]),
     "sumac_fill_zero": (i32, [p, i64, p]),
+    "sumac_init_factor": (i32, [p, p, p, i64, p, i32, f32, p, p]),
+    "sumac_init_scale_workspace_bytes": (sz, []),
+    "sumac_init_scale_terms": (i32, [p, p, i32, p, p, p, i64, p, p, sz, p]),
     "sumac_wait_flag": (i32, [p, p, u64, p]),
 }
 

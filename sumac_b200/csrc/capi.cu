@@ -704,6 +704,27 @@ int sumac_fill_zero(float* p, int64_t n, sumac_stream_t stream) {
   return launched("fill_zero");
 }
 
+// ------------------------------------------------------------------------------ initial factors
+int sumac_init_factor(const int32_t* rowptr, const int32_t* col, const float* val, int64_t M,
+                      const float* R, int d, float sign, float* out, sumac_stream_t stream) {
+  if (M < 0 || d <= 0 || (M > 0 && (!rowptr || !R || !out)))
+    return fail(SUMAC_ERR_ARG, "init_factor: bad args");
+  launch_init_spmm_sqrt(rowptr, col, val, M, R, d, sign, out, reinterpret_cast<cudaStream_t>(stream));
+  return launched("init_factor");
+}
+size_t sumac_init_scale_workspace_bytes(void) { return init_scale_workspace_bytes(); }
+int sumac_init_scale_terms(const float* A, const float* B, int d, const int32_t* ei,
+                           const int32_t* ej, const float* v, int64_t nnz, double* out, void* ws,
+                           size_t ws_bytes, sumac_stream_t stream) {
+  if (d <= 0 || nnz < 0 || !out || (nnz > 0 && (!A || !B || !ei || !ej || !v)))
+    return fail(SUMAC_ERR_ARG, "init_scale_terms: bad args");
+  if (!ws || ws_bytes < init_scale_workspace_bytes())
+    return fail(SUMAC_ERR_WORKSPACE, "init_scale_terms: workspace too small");
+  launch_init_scale_terms(A, B, d, ei, ej, v, nnz, static_cast<double*>(ws), out,
+                          reinterpret_cast<cudaStream_t>(stream));
+  return launched("init_scale_terms");
+}
+
 int sumac_wait_flag(const int* flag, int* dev_err, unsigned long long timeout_ns,
                     sumac_stream_t stream) {
   if (!flag || !dev_err) return fail(SUMAC_ERR_ARG, "wait_flag: null pointer");

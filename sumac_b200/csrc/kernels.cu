@@ -856,8 +856,23 @@ __global__ void perm_inv_kernel(const int64_t* __restrict__ perm, int64_t m, int
   if (blockIdx.x == 0 && threadIdx.x == 0) *ntask = 0;
 }
 
+// The lanes of the warp holding the same value v (0 <= v < 2^nbits): one ballot per bit (warp
+// multisplit). Every lane must call it.
+__device__ __forceinline__ unsigned warp_peers(int v, int nbits) {
+  unsigned peers = 0xffffffffu;
+  for (int i = 0; i < nbits; ++i) {
+    const bool bit = (v >> i) & 1;
+    const unsigned bal = __ballot_sync(0xffffffffu, bit);
+    peers &= bit ? bal : ~bal;
+  }
+  return peers;
+}
+
+// Bits of the block index, with nb itself as the value of a missing edge.
+static int csr_block_bits(int nb) { return 32 - __builtin_clz((unsigned)nb); }
+
 __global__ void csr_hist_kernel(const int32_t* __restrict__ e_fixed, int64_t nnz, int64_t chunk,
-                                const int32_t* __restrict__ inv, int bs, int nb,
+                                const int32_t* __restrict__ inv, int bs, int nb, int nbits,
                                 int32_t* __restrict__ hist) {
   extern __shared__ int sh[];
   for (int k = threadIdx.x; k < nb; k += blockDim.x) sh[k] = 0;
@@ -875,10 +890,10 @@ __global__ void csr_hist_kernel(const int32_t* __restrict__ e_fixed, int64_t nnz
     }
 #pragma unroll
     for (int j = 0; j < IT; ++j) {
-      const int blk = fx[j] >= 0 ? inv[fx[j]] / bs : -1;
+      const int blk = fx[j] >= 0 ? inv[fx[j]] / bs : nb;
       // one shared-memory atomic per distinct block in the warp
-      const unsigned peers = __match_any_sync(0xffffffffu, blk);
-      if (blk >= 0 && (peers & lane_lt) == 0) atomicAdd(&sh[blk], __popc(peers));
+      const unsigned peers = warp_peers(blk, nbits);
+      if (blk < nb && (peers & lane_lt) == 0) atomicAdd(&sh[blk], __popc(peers));
     }
   }
   __syncthreads();
@@ -942,25 +957,54 @@ __global__ void csr_scan_add_kernel(int32_t* __restrict__ hist, int ncta,
   for (int i = threadIdx.x; i < ncta; i += blockDim.x) row[i] += base;
 }
 
-// Scatter with IT edges per thread per round (up to 256 * IT edges in flight per CTA). Within a
-// round the edges are ordered item-major (edge rb + j * 256 + t is item j of thread t), and a
-// block's positions follow that order: the count of each (item, warp) segment is scanned per
-// block in shared memory. Keeps the stable order of the single-item scatter below.
+// Exclusive scan over the 256 threads of a CTA; *total gets the sum. Two barriers.
+__device__ __forceinline__ int block_exclusive_scan_256(int v, int* wsum, int* total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) wsum[w] = incl;
+  __syncthreads();
+  int before = 0, all = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int ws = wsum[i];
+    before += i < w ? ws : 0;
+    all += ws;
+  }
+  *total = all;
+  __syncthreads();  // wsum is reused by the next call
+  return before + incl - v;
+}
+
+// Stable partition of the edges by block, IT edges per thread per round (256 * IT edges per CTA
+// and round). Within a round the edges are ordered item-major (edge rb + j * 256 + t is item j of
+// thread t): segment s = j * 8 + warp holds 32 consecutive edges. Warp multisplit gives each
+// edge its rank among the segment's edges of its block and the segment's count per block; one
+// CTA-wide exclusive scan of the counts in block-major order [block][segment] then gives every
+// edge its position behind the block's earlier rounds. Same order (and output) as
+// csr_scatter_kernel.
 template <int IT>
 __global__ void __launch_bounds__(256)
-    csr_scatter_multi_kernel(const int32_t* __restrict__ e_fixed, const int32_t* __restrict__ e_out,
-                             const float* __restrict__ e_val, int64_t nnz, int64_t chunk,
-                             const int32_t* __restrict__ inv, int bs, int nb, int64_t M,
-                             const int32_t* __restrict__ offs, int32_t* __restrict__ keys,
-                             int2* __restrict__ ent) {
-  constexpr int S = IT * 8;  // (item, warp) segments per round
+    csr_scatter_tile_kernel(const int32_t* __restrict__ e_fixed, const int32_t* __restrict__ e_out,
+                            const float* __restrict__ e_val, int64_t nnz, int64_t chunk,
+                            const int32_t* __restrict__ inv, int bs, int nb, int nbits, int64_t M,
+                            const int32_t* __restrict__ offs, int32_t* __restrict__ keys,
+                            int2* __restrict__ ent) {
+  constexpr int S = IT * 8;
   extern __shared__ int sm[];
-  int* base = sm;             // [nb] next free position of each block
-  int* cnt = sm + nb;         // [nb][S] segment counts (zero between rounds)
-  int* pre = cnt + nb * S;    // [nb][S] segment start positions of this round
+  int* base = sm;        // [nb] next free position of each block
+  int* cnt = sm + nb;    // [nb][S] segment counts, then their exclusive prefix
+  __shared__ int wsum[8];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ns = nb * S;
+  const int per = (ns + 255) / 256;  // scan elements per thread (contiguous)
+  const int k0 = min(ns, (int)threadIdx.x * per), k1 = min(ns, k0 + per);
   for (int k = threadIdx.x; k < nb; k += blockDim.x) base[k] = offs[(int64_t)k * gridDim.x + blockIdx.x];
-  for (int k = threadIdx.x; k < nb * S; k += blockDim.x) cnt[k] = 0;
+  for (int k = threadIdx.x; k < ns; k += blockDim.x) cnt[k] = 0;
   __syncthreads();
   const int64_t e0 = (int64_t)blockIdx.x * chunk;
   const int64_t e1 = min(nnz, e0 + chunk);
@@ -978,44 +1022,52 @@ __global__ void __launch_bounds__(256)
         const int pos = inv[blk[j]];
         blk[j] = pos / bs;
         loc[j] = pos - blk[j] * bs;
+      } else {
+        blk[j] = nb;
+        loc[j] = 0;
       }
     }
 #pragma unroll
     for (int j = 0; j < IT; ++j) {
-      const unsigned peers = __match_any_sync(0xffffffffu, blk[j]);
+      const unsigned peers = warp_peers(blk[j], nbits);
       rank[j] = __popc(peers & lt_mask);
-      if (blk[j] >= 0 && rank[j] == 0) cnt[blk[j] * S + j * 8 + warp] = __popc(peers);
+      if (blk[j] < nb && rank[j] == 0) cnt[blk[j] * S + j * 8 + warp] = __popc(peers);
     }
     __syncthreads();
-    // per block: exclusive scan of its S segment counts on top of its running base
-    for (int b = warp; b < nb; b += 8) {
-      int v0 = lane < S ? cnt[b * S + lane] : 0;
-      int v1 = lane + 32 < S ? cnt[b * S + lane + 32] : 0;
-      int i0 = v0, i1 = v1;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int t0 = __shfl_up_sync(0xffffffffu, i0, o);
-        const int t1 = __shfl_up_sync(0xffffffffu, i1, o);
-        if (lane >= o) { i0 += t0; i1 += t1; }
-      }
-      const int tot0 = __shfl_sync(0xffffffffu, i0, 31);
-      const int tot1 = __shfl_sync(0xffffffffu, i1, 31);
-      const int run = base[b];
-      if (lane < S) { pre[b * S + lane] = run + i0 - v0; cnt[b * S + lane] = 0; }
-      if (lane + 32 < S) { pre[b * S + lane + 32] = run + tot0 + i1 - v1; cnt[b * S + lane + 32] = 0; }
-      __syncwarp();
-      if (lane == 0) base[b] = run + tot0 + tot1;
+    int tsum = 0;
+    for (int k = k0; k < k1; ++k) tsum += cnt[k];
+    int total;
+    int run = block_exclusive_scan_256(tsum, wsum, &total);
+    for (int k = k0; k < k1; ++k) {
+      const int v = cnt[k];
+      cnt[k] = run;
+      run += v;
     }
     __syncthreads();
 #pragma unroll
     for (int j = 0; j < IT; ++j) {
-      if (blk[j] >= 0) {
+      if (blk[j] < nb) {
         const int64_t e = rb + j * 256 + threadIdx.x;
-        const int pos = pre[blk[j] * S + j * 8 + warp] + rank[j];
-        keys[pos] = (int32_t)((int64_t)blk[j] * M + e_out[e]);
+        const int b = blk[j];
+        const int pos = base[b] + cnt[b * S + j * 8 + warp] - cnt[b * S] + rank[j];
+        keys[pos] = (int32_t)((int64_t)b * M + e_out[e]);
         ent[pos] = make_int2(loc[j], __float_as_int(e_val[e]));
       }
     }
+    // the blocks' new bases (read before any thread rewrites base or cnt)
+    int nbase[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int b = threadIdx.x + q * 256;
+      nbase[q] = b < nb ? base[b] + (b + 1 < nb ? cnt[(b + 1) * S] : total) - cnt[b * S] : 0;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int b = threadIdx.x + q * 256;
+      if (b < nb) base[b] = nbase[q];
+    }
+    for (int k = k0; k < k1; ++k) cnt[k] = 0;
     __syncthreads();
   }
 }
@@ -1156,19 +1208,28 @@ int launch_block_csr(const int64_t* perm, int64_t m_fixed, int num_blocks, const
   count_launch();
   perm_inv_kernel<<<grid_cap(m_fixed, 256, 148 * 8), 256, 0, stream>>>(perm, m_fixed, inv, ntask);
   if (nnz > 0) {
+    const int nbits = csr_block_bits(num_blocks);
     count_launch();
     csr_hist_kernel<<<L.ncta, CSR_THREADS, num_blocks * sizeof(int), stream>>>(
-        e_fixed, nnz, L.chunk, inv, bs, num_blocks, hist);
+        e_fixed, nnz, L.chunk, inv, bs, num_blocks, nbits, hist);
     count_launch();
     csr_scan_rows_kernel<<<num_blocks, 1024, 0, stream>>>(hist, L.ncta, totals);
     count_launch();
     csr_scan_add_kernel<<<num_blocks, 256, 0, stream>>>(hist, L.ncta, totals);
-    // four edges per thread per round while the block table fits comfortably in shared memory
-    const size_t smem4 = (size_t)(1 + 2 * 32) * num_blocks * sizeof(int);
+    // four (one) edges per thread per round while the block table fits in 48 KB of shared memory
+    // (up to 1024 blocks: the new bases are formed four per thread)
+    const size_t smem4 = (size_t)(1 + 32) * num_blocks * sizeof(int);
+    const size_t smem1 = (size_t)(1 + 8) * num_blocks * sizeof(int);
     if (smem4 <= 48 * 1024) {
       count_launch();
-      csr_scatter_multi_kernel<4><<<L.ncta, CSR_THREADS, smem4, stream>>>(
-          e_fixed, e_out, e_val, nnz, L.chunk, inv, bs, num_blocks, M, hist, keys, ent);
+      csr_scatter_tile_kernel<4><<<L.ncta, CSR_THREADS, smem4, stream>>>(
+          e_fixed, e_out, e_val, nnz, L.chunk, inv, bs, num_blocks, nbits, M, hist, keys, ent);
+      goto scattered;
+    }
+    if (smem1 <= 48 * 1024 && num_blocks <= 1024) {
+      count_launch();
+      csr_scatter_tile_kernel<1><<<L.ncta, CSR_THREADS, smem1, stream>>>(
+          e_fixed, e_out, e_val, nnz, L.chunk, inv, bs, num_blocks, nbits, M, hist, keys, ent);
       goto scattered;
     }
     {
@@ -1298,6 +1359,99 @@ void launch_sum_partials(const double* partials, int n, int w, double* out, int 
                          cudaStream_t stream) {
   count_launch();
   sum_partials_kernel<<<1, 32, 0, stream>>>(partials, n, w, out, accumulate);
+}
+
+// ============================================================================================
+// initial factors (training/salsa.py:36-78): out_r = sign sqrt(sum_e val_e R[col_e]) over the
+// entries e of row r (rows sorted, rowptr), i.e. sign sqrt(S R) row by row; and the three sums of
+// the closed-form scale: sum v^2, sum v L, sum L^2 with L_e = <A_i, B_j> over the entries (i, j, v)
+// ============================================================================================
+__global__ void __launch_bounds__(256) init_spmm_sqrt_kernel(const int32_t* __restrict__ rowptr,
+                                                             const int32_t* __restrict__ col,
+                                                             const float* __restrict__ val, int64_t M,
+                                                             const float* __restrict__ R, int d,
+                                                             float sign, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t r = w0; r < M; r += nw) {
+    const int e0 = rowptr[r], e1 = rowptr[r + 1];
+    for (int c0 = 0; c0 < d; c0 += 32) {
+      const int c = c0 + lane;
+      const bool on = c < d;
+      float acc = 0.f;
+      int e = e0;
+      for (; e + 4 <= e1; e += 4) {
+        int j[4];
+        float v[4], x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) { j[u] = col[e + u]; v[u] = val[e + u]; }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) x[u] = on ? R[(int64_t)j[u] * d + c] : 0.f;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) acc = fmaf(v[u], x[u], acc);
+      }
+      for (; e < e1; ++e) acc = fmaf(val[e], on ? R[(int64_t)col[e] * d + c] : 0.f, acc);
+      if (on) out[r * d + c] = sign * sqrtf(acc);
+    }
+  }
+}
+
+constexpr int INIT_SCALE_GRID = 148 * 4;
+
+__global__ void __launch_bounds__(256) init_scale_terms_kernel(
+    const float* __restrict__ A, const float* __restrict__ B, int d, const int32_t* __restrict__ ei,
+    const int32_t* __restrict__ ej, const float* __restrict__ v, int64_t nnz,
+    double* __restrict__ partials) {
+  double s_vv = 0.0, s_vl = 0.0, s_ll = 0.0;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < nnz;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const float* a = A + (int64_t)ei[e] * d;
+    const float* b = B + (int64_t)ej[e] * d;
+    float L = 0.f;
+#pragma unroll 4
+    for (int k = 0; k < d; ++k) L = fmaf(a[k], b[k], L);
+    const double x = v[e], l = L;
+    s_vv += x * x;
+    s_vl += x * l;
+    s_ll += l * l;
+  }
+  __shared__ double red[3][8];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    s_vv += __shfl_xor_sync(0xffffffffu, s_vv, o);
+    s_vl += __shfl_xor_sync(0xffffffffu, s_vl, o);
+    s_ll += __shfl_xor_sync(0xffffffffu, s_ll, o);
+  }
+  if ((threadIdx.x & 31) == 0) {
+    red[0][threadIdx.x >> 5] = s_vv;
+    red[1][threadIdx.x >> 5] = s_vl;
+    red[2][threadIdx.x >> 5] = s_ll;
+  }
+  __syncthreads();
+  if (threadIdx.x < 3) {
+    double t = 0.0;
+    for (int w = 0; w < 8; ++w) t += red[threadIdx.x][w];
+    partials[(int64_t)blockIdx.x * 3 + threadIdx.x] = t;
+  }
+}
+
+void launch_init_spmm_sqrt(const int32_t* rowptr, const int32_t* col, const float* val, int64_t M,
+                           const float* R, int d, float sign, float* out, cudaStream_t stream) {
+  if (M <= 0) return;
+  count_launch();
+  init_spmm_sqrt_kernel<<<grid_cap(M * 32, 256, 148 * 8), 256, 0, stream>>>(rowptr, col, val, M, R,
+                                                                            d, sign, out);
+}
+
+size_t init_scale_workspace_bytes() { return (size_t)INIT_SCALE_GRID * 3 * sizeof(double); }
+
+void launch_init_scale_terms(const float* A, const float* B, int d, const int32_t* ei,
+                             const int32_t* ej, const float* v, int64_t nnz, double* partials,
+                             double* out, cudaStream_t stream) {
+  count_launch();
+  init_scale_terms_kernel<<<INIT_SCALE_GRID, 256, 0, stream>>>(A, B, d, ei, ej, v, nnz, partials);
+  launch_sum_partials(partials, INIT_SCALE_GRID, 3, out, 0, stream);
 }
 
 // ============================================================================================

@@ -104,6 +104,14 @@ int launch_block_csr(const int64_t* perm, int64_t m_fixed, int num_blocks, const
                      const int32_t* e_out, const float* e_val, int64_t nnz, int64_t M,
                      int32_t* rowptr, int2* ent, void* ws, size_t ws_bytes, cudaStream_t stream);
 
+// ---- initial factors ----------------------------------------------------------------------
+void launch_init_spmm_sqrt(const int32_t* rowptr, const int32_t* col, const float* val, int64_t M,
+                           const float* R, int d, float sign, float* out, cudaStream_t stream);
+size_t init_scale_workspace_bytes();
+void launch_init_scale_terms(const float* A, const float* B, int d, const int32_t* ei,
+                             const int32_t* ej, const float* v, int64_t nnz, double* partials,
+                             double* out, cudaStream_t stream);
+
 // ---- metrics / loss -----------------------------------------------------------------------
 // partials[grid][6] doubles:
 //   sum M^2, sum (v-M)^2, sum (v-L)^2, sum min(v, M), sum v, sum v^2    (M = ReLU(L))

@@ -53,10 +53,11 @@ class SparseDirection:
     ``out`` the rows of the updated factor (M of them), sorted stably by ``out``."""
 
     def __init__(self, fixed: Tensor, out: Tensor, val: Tensor, m_fixed: int, M: int,
-                 num_blocks: int):
-        order = torch.sort(out, stable=True).indices
-        self.fixed = fixed[order].to(torch.int32).contiguous()
-        self.out = out[order].to(torch.int32).contiguous()
+                 num_blocks: int, csr: bool = True):
+        # a stable radix sort of 32-bit keys (half the passes of int64 keys)
+        out_sorted, order = torch.sort(out.to(torch.int32), stable=True)
+        self.out = out_sorted.contiguous()
+        self.fixed = fixed.to(torch.int32)[order].contiguous()
         self.val = val[order].to(torch.float32).contiguous()
         self.m_fixed = int(m_fixed)
         self.M = int(M)
@@ -64,8 +65,17 @@ class SparseDirection:
         self.num_blocks = int(num_blocks)
         self.block_size = (self.m_fixed + num_blocks - 1) // num_blocks
         dev = val.device
-        self.rowptr = torch.empty(num_blocks * self.M + 1, dtype=torch.int32, device=dev)
-        self.ent = torch.empty((max(self.nnz, 1), 2), dtype=torch.int32, device=dev)
+        self._out_rowptr = None
+        if csr:  # per-block CSR storage (rebuild)
+            self.rowptr = torch.empty(num_blocks * self.M + 1, dtype=torch.int32, device=dev)
+            self.ent = torch.empty((max(self.nnz, 1), 2), dtype=torch.int32, device=dev)
+
+    def out_rowptr(self) -> Tensor:
+        """[M + 1] int32: the entries of updated row r are [rowptr[r], rowptr[r + 1])."""
+        if self._out_rowptr is None:
+            q = torch.arange(self.M + 1, dtype=torch.int32, device=self.out.device)
+            self._out_rowptr = torch.searchsorted(self.out, q).to(torch.int32)
+        return self._out_rowptr
 
     def rebuild(self, perm: Tensor) -> None:
         """Per-block CSR for the row permutation ``perm`` of the fixed factor."""

@@ -219,3 +219,27 @@ def gather_owned_rows(local, lo, hi, rows, out):
     check(L.sumac_gather_owned_rows(ptr(local), int(lo), int(hi), ptr(rows), rows.numel(),
                                     local.shape[1], ptr(out), N.stream_ptr(out.device)),
           "gather_owned_rows")
+
+
+def init_factor(rowptr, col, val, R, sign):
+    """sign * sqrt(S R) row by row, S given by its row-sorted entries (rowptr[M+1], col, val)
+    (the sparse products of init_salsa_factors, training/salsa.py:46-50)."""
+    R = _cuda_f32("R", R)
+    M, d = rowptr.numel() - 1, R.shape[1]
+    out = torch.empty((M, d), dtype=torch.float32, device=R.device)
+    check(N.lib().sumac_init_factor(ptr(rowptr), ptr(col), ptr(val), M, ptr(R), d, float(sign),
+                                    ptr(out), N.stream_ptr(R.device)), "init_factor")
+    return out
+
+
+def init_scale_terms(A, B, ei, ej, v):
+    """float64 device tensor (sum v^2, sum v L, sum L^2), L = <A[ei], B[ej]> per entry (the sums
+    of the closed-form scale of init_salsa_factors, training/salsa.py:52-59)."""
+    A, B = _cuda_f32("A", A), _cuda_f32("B", B)
+    L = N.lib()
+    out = torch.empty(3, dtype=torch.float64, device=A.device)
+    nb = L.sumac_init_scale_workspace_bytes()
+    ws = _ws(A.device, nb, "init_scale")
+    check(L.sumac_init_scale_terms(ptr(A), ptr(B), A.shape[1], ptr(ei), ptr(ej), ptr(v), v.numel(),
+                                   ptr(out), ptr(ws), nb, N.stream_ptr(A.device)), "init_scale_terms")
+    return out

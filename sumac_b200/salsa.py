@@ -21,37 +21,85 @@ from .data import SparseDirection
 from .metrics import Evaluator
 
 
+def _tall_qr(A: Tensor) -> tuple[Tensor, Tensor] | None:
+    """Q, R of a tall, thin float matrix by Cholesky QR in float64: R^T R = A^T A, Q = A R^-1.
+    One d x d Gram product and a triangular solve instead of a Householder QR over m rows; in
+    float64 its accuracy loss (cond(A)^2 eps64) stays below float32 rounding for cond(A) up to
+    ~1e4 and well beyond. None when the Gram matrix is not numerically positive definite."""
+    A64 = A.double()
+    G = A64.T @ A64
+    L, info = torch.linalg.cholesky_ex(G)
+    if int(info.item()) != 0:
+        return None
+    R = L.T
+    Q = torch.linalg.solve_triangular(R, A64, upper=True, left=False)
+    return Q, R
+
+
 def refactor(A: Tensor, B: Tensor) -> tuple[Tensor, Tensor]:
-    """A B^T unchanged, singular values shared (training/salsa.py:20-33)."""
-    Qa, Ra = torch.linalg.qr(A, mode="reduced")
-    Qb, Rb = torch.linalg.qr(B, mode="reduced")
-    U, S, Vh = torch.linalg.svd(Ra @ Rb.T, full_matrices=False)
+    """A B^T unchanged, singular values shared (training/salsa.py:20-33): A = Qa U sqrt(S),
+    B = Qb V sqrt(S) from QR factorisations of A and B and the SVD of Ra Rb^T. On the GPU the QRs
+    are Cholesky QRs in float64 and the d x d SVD runs on the host: the result does not depend on
+    the QR's sign convention (U absorbs it), only, like the reference's, on the SVD's choice of
+    signs per singular pair."""
+    qa = _tall_qr(A) if A.is_cuda else None
+    qb = _tall_qr(B) if qa is not None else None
+    if qa is None or qb is None:
+        Qa, Ra = torch.linalg.qr(A, mode="reduced")
+        Qb, Rb = torch.linalg.qr(B, mode="reduced")
+        U, S, Vh = torch.linalg.svd(Ra @ Rb.T, full_matrices=False)
+        sqrtS = torch.diag(torch.sqrt(S))
+        return Qa @ U @ sqrtS, Qb @ Vh.T @ sqrtS
+    (Qa, Ra), (Qb, Rb) = qa, qb
+    U, S, Vh = torch.linalg.svd((Ra @ Rb.T).cpu(), full_matrices=False)
     sqrtS = torch.diag(torch.sqrt(S))
-    return Qa @ U @ sqrtS, Qb @ Vh.T @ sqrtS
+    Ua = (U @ sqrtS).to(A.device)
+    Vb = (Vh.T @ sqrtS).to(A.device)
+    return (Qa @ Ua).to(A.dtype), (Qb @ Vb).to(B.dtype)
 
 
-def init_salsa_factors(S_index, S_value, m, n, d, gen):
+def init_salsa_factors(S_index, S_value, m, n, d, gen, dirs=None):
     """A > 0, B < 0 from S times uniform noise, rescaled, then refactored
     (training/salsa.py:36-78); draws from `gen` in the same order as the reference. The uniform
     draws come from `gen` on its own device; the arithmetic runs on the device of S_value. The
     steps (sparse products, closed-form scale, QR + QR + SVD) are the reference's, in its order: the
-    same draws in the same order are what makes the initial factors match a reference run."""
+    same draws in the same order are what makes the initial factors match a reference run.
+
+    On the GPU the sparse products and the scale's sums are native kernels over the entries
+    sorted by row and by column (`dirs` = the (A-update, B-update) SparseDirection pair when the
+    caller has them, else they are built here); on the CPU it is the reference's torch code."""
     device, dtype = S_value.device, S_value.dtype
-    with torch.sparse.check_sparse_tensor_invariants(False):
-        S = torch.sparse_coo_tensor(S_index.to(device=device, dtype=torch.long), S_value,
-                                    size=(m, n), device=device, dtype=dtype).coalesce()
-        R_A = torch.rand((n, d), device=gen.device, dtype=dtype, generator=gen).to(device)
-        R_B = torch.rand((m, d), device=gen.device, dtype=dtype, generator=gen).to(device)
-        A = torch.sqrt(torch.sparse.mm(S, R_A))
-        B = -torch.sqrt(torch.sparse.mm(S.T, R_B))
-    Lij = torch.sum(A[S_index[0], :] * B[S_index[1], :], dim=1)
-    ssqS = torch.sum(S_value ** 2)
-    ssqL = torch.sum(Lij ** 2)
-    SdotL = torch.sum(S_value * Lij)
+    R_A = torch.rand((n, d), device=gen.device, dtype=dtype, generator=gen).to(device)
+    R_B = torch.rand((m, d), device=gen.device, dtype=dtype, generator=gen).to(device)
+    if device.type == "cuda" and dtype == torch.float32:
+        if dirs is None:
+            dirs = (SparseDirection(S_index[1], S_index[0], S_value, n, m, 1, csr=False),
+                    SparseDirection(S_index[0], S_index[1], S_value, m, n, 1, csr=False))
+        dir_a, dir_b = dirs
+        A = ops.init_factor(dir_a.out_rowptr(), dir_a.fixed, dir_a.val, R_A, 1.0)
+        B = ops.init_factor(dir_b.out_rowptr(), dir_b.fixed, dir_b.val, R_B, -1.0)
+        ssqS, SdotL, ssqL = ops.init_scale_terms(A, B, dir_a.out, dir_a.fixed, dir_a.val)
+    else:
+        with torch.sparse.check_sparse_tensor_invariants(False):
+            S = torch.sparse_coo_tensor(S_index.to(device=device, dtype=torch.long), S_value,
+                                        size=(m, n), device=device, dtype=dtype).coalesce()
+            A = torch.sqrt(torch.sparse.mm(S, R_A))
+            B = -torch.sqrt(torch.sparse.mm(S.T, R_B))
+        Lij = torch.sum(A[S_index[0], :] * B[S_index[1], :], dim=1)
+        ssqS = torch.sum(S_value ** 2)
+        ssqL = torch.sum(Lij ** 2)
+        SdotL = torch.sum(S_value * Lij)
     a, b, c = ssqL, -2.0 * SdotL, -3.0 * ssqS
     alpha = (-b + torch.sqrt(b ** 2 - 4 * a * c)) / (2 * a)
-    scale = torch.clamp(torch.sqrt(alpha), 0.0, 1.0)
+    scale = torch.clamp(torch.sqrt(alpha), 0.0, 1.0).to(dtype)
     return refactor(scale * A, scale * B)
+
+
+def make_directions(S_index, S_value, m, n, num_blocks):
+    """(A-update, B-update) edge sets: the A-update's fixed rows are the rows of B (columns of S)
+    and its updated rows the rows of S; the B-update's the other way round."""
+    return (SparseDirection(S_index[1], S_index[0], S_value, n, m, num_blocks),
+            SparseDirection(S_index[0], S_index[1], S_value, m, n, num_blocks))
 
 
 def draw_perm(m: int, gen: torch.Generator, device) -> Tensor:
@@ -66,10 +114,13 @@ def unbias_values(momentum: float, first_step: int, count: int) -> np.ndarray:
                      for s in range(first_step, first_step + count)], dtype=np.float32)
 
 
+GRAPH_MIN_ITERATIONS = 40
+
+
 class SalsaState:
     """Device state of one SALSA run: padded factors, momentum, both directions' CSR."""
 
-    def __init__(self, S_index, S_value, m, n, cfg: SumacConfig, A, B):
+    def __init__(self, S_index, S_value, m, n, cfg: SumacConfig, A, B, dirs=None):
         dev = cfg.device
         self.d = cfg.rank
         self.Dp = ops.padded_rank(self.d)
@@ -80,10 +131,9 @@ class SalsaState:
         self.Bp = ops.pad_factor(B.to(torch.float32), self.Dp)
         self.dA = torch.zeros_like(self.Ap)
         self.dB = torch.zeros_like(self.Bp)
-        # B-update: fixed = rows of A (S rows), updated rows = columns of S
-        self.dir_b = SparseDirection(S_index[0], S_index[1], S_value, m, n, self.nb)
-        # A-update: fixed = rows of B (S columns), updated rows = rows of S
-        self.dir_a = SparseDirection(S_index[1], S_index[0], S_value, n, m, self.nb)
+        if dirs is None:
+            dirs = make_directions(S_index, S_value, m, n, self.nb)
+        self.dir_a, self.dir_b = dirs
         self.momentum = float(cfg.momentum)
         self.lrate = float(np.float32(cfg.learning_rate))
         self.unbias = torch.empty(self.nb, dtype=torch.float32, device=dev)
@@ -161,11 +211,15 @@ def salsa_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfi
     dev = cfg.device
     S_index = S_index.to(dev)
     S_value = S_value.to(dev)
+    dirs = make_directions(S_index, S_value, m, n, cfg.num_blocks)
     if A_init is None or B_init is None:
-        A, B = init_salsa_factors(S_index, S_value, m, n, cfg.rank, gen)
+        A, B = init_salsa_factors(S_index, S_value, m, n, cfg.rank, gen, dirs=dirs)
     else:
         A, B = A_init.to(dev), B_init.to(dev)
-    st = SalsaState(S_index, S_value, m, n, cfg, A, B)
+    st = SalsaState(S_index, S_value, m, n, cfg, A, B, dirs=dirs)
+    # a CUDA graph of the iteration pays off over many iterations only (capturing ~800 launches
+    # costs about two iterations; a replay saves ~5 % of one)
+    st.use_graph = cfg.max_iterations >= GRAPH_MIN_ITERATIONS
     evaluator = Evaluator(S_index, S_value, cfg.rank, st.prec)
     # the reference's datasets draw one permutation each at construction (datasets.py:34)
     draw_perm(m, gen_rows, dev)

@@ -81,7 +81,8 @@ def test_masked_product(d, N, M, nnz, prec):
 @pytest.mark.parametrize("m_fixed,M,nb,nnz", [(57, 40, 5, 300), (1000, 777, 13, 40000),
                                               (5000, 3000, 100, 200000), (64, 9, 64, 0),
                                               (300, 5000, 7, 2000), (5000, 800, 300, 30000),
-                                              (20000, 9000, 150, 2000000)])
+                                              (20000, 9000, 150, 2000000),
+                                              (5000, 800, 600, 30000), (6000, 500, 1500, 30000)])
 def test_block_csr_bit_exact(m_fixed, M, nb, nnz):
     rng = np.random.default_rng(m_fixed + nb)
     fi, oj, v = random_edges(rng, m_fixed, M, nnz)
