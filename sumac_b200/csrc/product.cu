@@ -424,13 +424,13 @@ int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float*
 }  // namespace sb
 
 #ifdef SB_TRACE
-// Copy the CTA-0 timeline of the last product / reduce launch (24 x 512 clock64 stamps).
+// Copy the CTA-0 timeline of the last product / reduce launch (28 x 512 clock64 stamps).
 extern "C" int sumac_debug_trace(unsigned long long* host_dst) {
   cudaDeviceSynchronize();
   return (int)cudaMemcpyFromSymbol(host_dst, sb::g_sb_trace, sizeof(sb::g_sb_trace));
 }
 extern "C" int sumac_debug_trace_clear(void) {
-  static unsigned long long zero[24][512];
+  static unsigned long long zero[28][512];
   return (int)cudaMemcpyToSymbol(sb::g_sb_trace, zero, sizeof(zero));
 }
 #endif

@@ -16,19 +16,24 @@
 // and one chunk) run chunk-major: (c0, tile 0), (c0, tile 1), ..., (c1 - 1, last tile). Each
 // tile has its own Y accumulator in TMEM (G x Dp columns), next to NBUF S buffers.
 //
-//   warp 0       TMA producer: lanes 0..15 fill each stage (F chunk, C^T chunk) together, one
-//                copy per lane; lane 16 + g owns X slot g. Copies issued by one thread complete
-//                one after another, copies from different lanes overlap.
+//   warp 0       TMA producer of the chunks: lanes 0..15 fill each stage (F chunk, C^T chunk)
+//                together, one copy per lane (copies issued by one thread complete one after
+//                another, copies from different lanes overlap)
 //   warp 1       first-MMA issuer (one thread): S = X_g F_c^T into the next of NBUF TMEM
-//                buffers (kind::tf32); in TF32 reduce mode warp 10 issues the odd pairs
-//   warps 2..9   epilogue, two warps per TMEM lane quadrant, each on half of the columns:
-//                tcgen05.ld S -> ReLU -> tcgen05.st R (or accumulate the sums); at the end of a
-//                group tcgen05.ld of each Y_g -> global
-//   warp 10      3xTF32: splits each X tile into tf32 hi / lo halves in shared memory;
-//                TF32 product: converts each C chunk to fp16 for the second MMA
+//                buffers (kind::tf32); with an even NBUF >= 4 in TF32 mode a second issuer takes
+//                the odd pairs
+//   warps 2..9   epilogue, two warps per TMEM lane quadrant, each on half of the columns: they
+//                prepare the group's X tiles in shared memory (round / scale / split) two pairs
+//                ahead of the first chunk's pairs, then per pair tcgen05.ld S -> ReLU ->
+//                tcgen05.st R (or accumulate the sums), and in the last chunk tcgen05.ld of each
+//                Y_g -> global behind the next tile's pair
+//   warp 10      TF32: chunk prep (fp16 copy of the C chunk in product mode; rounding of F where
+//                it was not packed as tf32 values)
 //   warps 11-12  second-MMA issuers (one thread each, product mode, even / odd tiles of the
 //                group): Y_g += R C_c with R read from TMEM once the epilogue has rewritten
 //                that S as R = ReLU(S); the commit hands the S buffer back to warp 1.
+//   X loader     (last warp; warp 10 in 3xTF32 mode) loads each group's row tiles into its X
+//                slot set (two sets where they fit, so the next group's tiles land early)
 //
 // Cost model (measured on B200 with in-kernel timestamps): at small rank the kernel is bound by
 // serial latencies, not by tensor throughput or HBM: ~50 ns per tcgen05 MMA or commit issued by
@@ -57,7 +62,7 @@ namespace sb {
 // Optional in-kernel timeline (build with -DSB_TRACE): CTA 0 stamps clock64() at each hand-off of
 // the pipeline into g_sb_trace[event][index]; sumac_debug_trace copies it out. Off by default.
 #ifdef SB_TRACE
-__device__ unsigned long long g_sb_trace[24][512];
+__device__ unsigned long long g_sb_trace[28][512];
 #define SB_TR(ev, i)                                                         \
   do {                                                                       \
     if (blockIdx.x == 0 && (unsigned)(i) < 512u) g_sb_trace[ev][i] = clock64(); \
@@ -122,9 +127,21 @@ struct ProductCfg {
   static constexpr int C16_BYTES = H16 ? DP * BN * 2 : 0;         // fp16 copy of the C chunk
   static constexpr int STAGE_ALLOC = STAGE_BYTES + C16_BYTES;
   static constexpr int XBUF_BYTES = NPREC * X_BYTES;      // one X slot (hi [, lo])
-  static constexpr int X_TOTAL = G * XBUF_BYTES;
+  // Beside the barriers: TMEM slot, abort flag, the epilogue's reduction scratch and (TF32
+  // product) the per-row scale exponents of two groups
+  static constexpr int aux_bytes(int xb) {
+    return ((3 * STAGES + 3 * 8 + 3 * xb * G + 2 * G + 4) * 8 + 16 + 8 * 3 * 8 +
+            (H16 ? 2 * G * 128 : 0) + 127) / 128 * 128;
+  }
+  // X slot sets: two when they fit next to the stages, so that the X loader brings in the next
+  // group's tiles while the current group runs; one otherwise
+  static constexpr int XB =
+      2 * G * XBUF_BYTES + STAGES * STAGE_ALLOC + aux_bytes(2) + 1024 <= 232448 ? 2 : 1;
+  static constexpr int AUX_BYTES = aux_bytes(XB);
+  static constexpr int NXS = XB * G;                      // X slots
+  static constexpr int X_TOTAL = NXS * XBUF_BYTES;
   static constexpr int SMEM_DATA = X_TOTAL + STAGES * STAGE_ALLOC;
-  static constexpr int SMEM_BYTES_RAW = SMEM_DATA + 1024 /*barriers*/ + 1024 /*align slack*/;
+  static constexpr int SMEM_BYTES_RAW = SMEM_DATA + AUX_BYTES + 1024 /*align slack*/;
   // at least 120 KB so that only one CTA (and one 512-column TMEM allocation) lives on an SM
   static constexpr int SMEM_BYTES = SMEM_BYTES_RAW < 122880 ? 122880 : SMEM_BYTES_RAW;
   static_assert(SMEM_BYTES_RAW <= 232448, "shared memory budget");
@@ -158,7 +175,6 @@ struct ProductCfg {
   // -2^-12 per operand): the X tiles by the epilogue warps when a group starts, each (F, C) chunk
   // by the chunk-prep warp, which in product mode also builds the fp16 copy of C
   static constexpr bool ROUND = !X3;
-  static constexpr bool AUX = X3 || !REDUCE;              // warp 10: X splitter / chunk prep
   static constexpr int CPREP_WARP = REDUCE ? 11 : 10;     // chunk-prep warp (ROUND)
   static_assert(!H16 || BN % 64 == 0, "the fp16 C chunk is built of 64-element sub-tiles");
   // product mode: second-MMA issuers, warp MMA2_WARP + i takes the tiles gi with gi % N2 == i
@@ -181,10 +197,21 @@ struct ProductCfg {
   static_assert(NBUF % N1 == 0, "S buffers split evenly between the first-MMA issuers");
   static_assert(REDUCE || MS == 2 || NBUF >= 2 * N2 - 1, "barrier phase lag");
   static_assert(MS == 1 || MS == N2, "one accumulator set per second-MMA issuer");
+  // X-loader warp: loads each group's row tiles into its X slot set (the epilogue warps prepare
+  // them); warp 10 in 3xTF32 mode (no chunk prep there), else the last warp
+  static constexpr int XLOAD_WARP =
+      X3 ? 10 : (REDUCE ? 12 : MMA2_WARP + N2 + (N1 == 2 ? 1 : 0));
   static constexpr int THREADS =
-      REDUCE ? 32 * (X3 ? 11 : 12) : 32 * (MMA2_WARP + N2 + (N1 == 2 ? 1 : 0));
-  // mbarriers, TMEM slot and abort flag sit below the epilogue's reduction scratch at +768 B
-  static_assert((3 * STAGES + 3 * NBUF + 5 * G + N1 + N2 + 1) * 8 + 8 <= 768, "barrier area");
+      32 * (REDUCE ? (X3 ? 11 : 13) : MMA2_WARP + N2 + (N1 == 2 ? 1 : 0) + (X3 ? 0 : 1));
+  static_assert(XLOAD_WARP < THREADS / 32, "X-loader warp");
+  // mbarriers (below +BAR_BYTES), then TMEM slot and abort flag, the epilogue's reduction scratch
+  // and the row exponents
+  static constexpr int NBARS = 3 * STAGES + 3 * NBUF + 3 * NXS + 2 * G + N1 + N2;
+  static constexpr int BAR_BYTES = (NBARS * 8 + 15) / 16 * 16;
+  static constexpr int RED_OFF = BAR_BYTES + 16;
+  static constexpr int ER_OFF = RED_OFF + EPI_WARPS * 3 * 8;
+  static constexpr bool ROW_SCALE = H16;  // per-row exponents kept for the Y readout
+  static_assert(ER_OFF + (ROW_SCALE ? 2 * G * TM : 0) <= AUX_BYTES, "auxiliary area");
   static constexpr int EPI_COLS = BN / 2;                 // S columns per epilogue warp
   static_assert(EPI_COLS % 16 == 0, "epilogue column split");
   static constexpr int LDW = EPI_COLS % 32 == 0 ? 32 : 16;  // tcgen05.ld/st width used
@@ -272,7 +299,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
-  uint8_t* sX = smem;                                   // [G][NPREC][X_BYTES]
+  uint8_t* sX = smem;                                   // [NXS][NPREC][X_BYTES]
   uint8_t* sStage = smem + Cfg::X_TOTAL;                // [STAGES][STAGE_ALLOC]
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Cfg::SMEM_DATA);
   uint64_t* full = bars;                    // [STAGES] TMA landed
@@ -281,16 +308,16 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
   uint64_t* s_full = c16_ready + STAGES;    // [NBUF] S = X F^T computed
   uint64_t* r_ready = s_full + NBUF;        // [NBUF] epilogue done with the S buffer
   uint64_t* s_free = r_ready + NBUF;        // [NBUF] second MMA done with the S buffer
-  uint64_t* x_full = s_free + NBUF;         // [G] X slot landed
-  uint64_t* x_ready = x_full + G;           // [G] X slot split (3xTF32) or rounded (TF32)
-  uint64_t* x_empty = x_ready + G;          // [G] last MMA reading the X slot completed
-  uint64_t* y_full = x_empty + G;           // [G] Y accumulator complete
+  uint64_t* x_full = s_free + NBUF;         // [NXS] X slot landed
+  uint64_t* x_ready = x_full + Cfg::NXS;    // [NXS] X slot prepared (rounded / scaled / split)
+  uint64_t* x_empty = x_ready + Cfg::NXS;   // [NXS] last MMA reading the X slot completed
+  uint64_t* y_full = x_empty + Cfg::NXS;    // [G] Y accumulator complete
   uint64_t* y_empty = y_full + G;           // [G] Y accumulator read out
   uint64_t* drain = y_empty + G;            // [N1 + N2] each MMA thread's own MMAs completed
-  uint64_t* x_rounded = drain + Cfg::N1 + Cfg::N2;  // all epilogue warps rounded the group's X
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_rounded + 1);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::SMEM_DATA + Cfg::BAR_BYTES);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  double* red = reinterpret_cast<double*>(smem + Cfg::SMEM_DATA + 768);  // [EPI_WARPS][3]
+  double* red = reinterpret_cast<double*>(smem + Cfg::SMEM_DATA + Cfg::RED_OFF);  // [EPI_WARPS][3]
+  int8_t* er_s = reinterpret_cast<int8_t*>(smem + Cfg::SMEM_DATA + Cfg::ER_OFF);  // [2][G][128]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -307,15 +334,16 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
       mbar_init(&r_ready[b], Cfg::EPI_WARPS);
       mbar_init(&s_free[b], Cfg::MS);
     }
+    for (int xs = 0; xs < Cfg::NXS; ++xs) {
+      mbar_init(&x_full[xs], 1);
+      mbar_init(&x_ready[xs], Cfg::EPI_WARPS);
+      mbar_init(&x_empty[xs], Cfg::N1);
+    }
     for (int g = 0; g < G; ++g) {
-      mbar_init(&x_full[g], 1);
-      mbar_init(&x_ready[g], X3 ? 1 : Cfg::EPI_WARPS);
-      mbar_init(&x_empty[g], Cfg::N1);
       mbar_init(&y_full[g], Cfg::MS);
       mbar_init(&y_empty[g], Cfg::EPI_WARPS);
     }
     for (int i = 0; i < Cfg::N1 + Cfg::N2; ++i) mbar_init(&drain[i], 1);
-    mbar_init(x_rounded, Cfg::EPI_WARPS);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -391,16 +419,16 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
       const uint32_t sX_addr = smem_u32(sX);
       const uint32_t sSt_addr = smem_u32(sStage);
       uint32_t pair = 0, chunk = 0;
-      uint32_t slot_par = 0;  // bit g: parity of the number of earlier uses of X slot g
+      uint32_t slot_par = 0;  // bit xs: parity of the number of earlier uses of X slot xs
       bool ok = true;
-      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+      uint32_t li = 0;        // groups of this CTA so far
+      for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++li) {
         const WorkItem w = work_item(p, item);
-        // every issuer waits for all X slots of the group, even those it issues no pair on: the
-        // slots' release barrier (one commit per issuer) must not see a commit for this group
-        // before the previous group's phase has completed
-        for (int gi = 0; gi < w.ntiles && ok; ++gi)
-          if (!mbar_wait(&x_ready[gi], (slot_par >> gi) & 1u, abort_flag,
-                         p.err, DEV_TIMEOUT_X, p.timeout_ns)) ok = false;
+        const int xs0 = (int)(li % Cfg::XB) * G;  // this group's X slots: xs0 + gi
+        // a tile's slot is waited for right before its first pair; every issuer also waits for
+        // the slots it issues no pair on before its release commit below (the slot's barrier
+        // must not see a commit for this group before the previous group's phase completed)
+        uint32_t waited = 0;
         for (int ci = 0; ci < w.c1 - w.c0 && ok; ++ci, ++chunk) {
           const int c = chunk_at(w, ci);
           const int stage = chunk % STAGES;
@@ -420,9 +448,14 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
               ok = false;
               break;
             }
+            if (!((waited >> gi) & 1u)) {
+              if (!mbar_wait(&x_ready[xs0 + gi], (slot_par >> (xs0 + gi)) & 1u, abort_flag, p.err,
+                             DEV_TIMEOUT_X, p.timeout_ns)) { ok = false; break; }
+              waited |= 1u << gi;
+            }
             tc_fence_after();
             SB_TR(1, pair);
-            const uint32_t xaddr = sX_addr + gi * Cfg::XBUF_BYTES;
+            const uint32_t xaddr = sX_addr + (xs0 + gi) * Cfg::XBUF_BYTES;
             const uint32_t s_tm = tbase + buf * BN;
 #pragma unroll
             for (int kk = 0; kk < DP / 8; ++kk) {
@@ -450,9 +483,13 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           // reduce mode: the first MMAs are the stage's only readers
           if (REDUCE && ok) mma_commit(&empty[stage]);
         }
-        if (ok)
-          for (int gi = 0; gi < w.ntiles; ++gi) mma_commit(&x_empty[gi]);  // X slots done
-        slot_par ^= (1u << w.ntiles) - 1u;
+        for (int gi = 0; gi < w.ntiles && ok; ++gi) {
+          if (!((waited >> gi) & 1u) &&
+              !mbar_wait(&x_ready[xs0 + gi], (slot_par >> (xs0 + gi)) & 1u, abort_flag, p.err,
+                         DEV_TIMEOUT_X, p.timeout_ns)) { ok = false; break; }
+          mma_commit(&x_empty[xs0 + gi]);  // X slot done
+        }
+        slot_par ^= ((1u << w.ntiles) - 1u) << xs0;
       }
       // make sure every MMA this thread issued has completed before TMEM is released
       mma_commit(&drain[me1]);
@@ -549,110 +586,144 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
     const int row_in_tile = qd * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(qd * 32) << 16;
     uint32_t pair = 0;
-    uint32_t slot_par = 0;
+    uint32_t slot_par = 0;       // bit g: parity of the earlier uses of Y slot g
+    uint32_t xslot_par = 0;      // bit xs: parity of the earlier uses of X slot xs
     double acc_s = 0.0, acc_s2 = 0.0, acc_n = 0.0;
     bool ok = true;
-    // fp16 second MMA: C is scaled by 2^ec (fixed per launch), row j of R by 2^er(j); read
-    // after the first X tiles are requested (a cold global load)
+    // fp16 second MMA: C is scaled by 2^ec (fixed per launch), row j of R by 2^er(j)
     int ec = 0;
-    float fmax = 0.f;
-    bool stats_read = false;
-    uint32_t xuses = 0;  // warp 2, lane g: loads issued into X slot g
-    uint32_t items_done = 0;  // groups this CTA finished (phase of x_rounded)
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+    float fmax = 0.f;  // max_i |F_i| (row norms), for the row scales
+    if constexpr (Cfg::H16) {
+      fmax = __uint_as_float(p.stats[0]);
+      const float cmax = __uint_as_float(p.stats[1]);
+      int ex = 0;
+      if (cmax > 0.f) frexpf(cmax, &ex);
+      ec = 14 - ex;
+    }
+    uint32_t li = 0;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++li) {
       const WorkItem w = work_item(p, item);
-      if (warp == 2) {
-        // lane g loads the group's tile g into X slot g once the slot's previous group is done
-        bool xok = true;
-        if (lane < w.ntiles) {
-          if (xuses > 0)
-            xok = mbar_wait(&x_empty[lane], (xuses - 1) & 1, abort_flag, p.err, DEV_TIMEOUT_X,
-                            p.timeout_ns);
-          if (xok) {
-            uint8_t* xdst = sX + lane * Cfg::XBUF_BYTES;
-            mbar_arrive_expect_tx(&x_full[lane], Cfg::X_BYTES);
-#pragma unroll
-            for (int s = 0; s < Cfg::KSUB; ++s)
-              tma_load_2d(xdst + s * Cfg::TM * Cfg::XW, &tmX, s * Cfg::BOX_K,
-                          (w.tile0 + lane) * Cfg::TM, &x_full[lane]);
-            ++xuses;
-            SB_TR(14, lane);
+      const int xs0 = (int)(li % Cfg::XB) * G;
+      const int split = item % p.splits;
+      // Prepare tile g of the group in shared memory, all 256 epilogue threads on it: 3xTF32
+      // splits X into tf32 hi / lo halves, TF32 rounds it to tf32; the TF32 product first scales
+      // row j by 2^er(j) so that S and R come out inside the fp16 range of the second MMA
+      // (|S_ji| <= |x_j| max_i |F_i| < 2^15 after scaling) and keeps er(j) for the Y readout (two
+      // sets of exponents, by group parity).
+      auto prep_tile = [&](int g) -> bool {
+        const int xs = xs0 + g;
+        if (!warp_wait(&x_full[xs], (xslot_par >> xs) & 1u, abort_flag, p.err, DEV_TIMEOUT_X,
+                       p.timeout_ns)) return false;
+        uint8_t* xt = sX + xs * Cfg::XBUF_BYTES;
+        const int et = threadIdx.x - 64;  // epilogue thread 0..255
+        if constexpr (X3) {
+          float4* xh = reinterpret_cast<float4*>(xt);
+          float4* xl = reinterpret_cast<float4*>(xt + Cfg::X_BYTES);
+#pragma unroll 2
+          for (int i = et; i < Cfg::X_BYTES / 16; i += Cfg::EPI_THREADS) {
+            const float4 v = xh[i];
+            const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
+            xh[i] = h;
+            xl[i] = make_float4(tf32_lo(v.x, h.x), tf32_lo(v.y, h.y), tf32_lo(v.z, h.z),
+                                tf32_lo(v.w, h.w));
           }
-        }
-        if (!__all_sync(0xffffffffu, xok)) { ok = false; break; }
-      }
-      int er[G];
+        } else if constexpr (Cfg::ROW_SCALE) {
+          // UPR consecutive threads share a row, one 16-byte unit each (within a row the swizzle
+          // only permutes the units)
+          constexpr int UPR = DP / 4;
+          constexpr int UPS = Cfg::XW / 16;  // units per row of one 128 B sub-tile
+          static_assert(UPR <= 32 && 32 % UPR == 0 && (Cfg::TM * UPR) % Cfg::EPI_THREADS == 0,
+                        "units per row");
+          const int ers = ((li & 1) * G + g) * Cfg::TM;
 #pragma unroll
-      for (int g = 0; g < G; ++g) er[g] = 0;
-      if constexpr (Cfg::H16) {
-        // TF32 product: row j of X is scaled by 2^er(j) and rounded to tf32 in place, so that S
-        // and R come out scaled (|S_ji| <= |x_j| max_i |F_i| < 2^15 after scaling, inside the
-        // fp16 range of R) and the per-pair epilogue only converts. The exponent comes from the
-        // row's norm, read by both threads that own the row before either rewrites its half.
-        if (!stats_read) {
-          fmax = __uint_as_float(p.stats[0]);
-          const float cmax = __uint_as_float(p.stats[1]);
-          int ex = 0;
-          if (cmax > 0.f) frexpf(cmax, &ex);
-          ec = 14 - ex;
-          stats_read = true;
-        }
-        for (int g = 0; g < w.ntiles && ok; ++g) {
-          if (!warp_wait(&x_full[g], (slot_par >> g) & 1u, abort_flag, p.err, DEV_TIMEOUT_X,
-                         p.timeout_ns)) { ok = false; break; }
-          float n2 = 0.f;
-#pragma unroll
-          for (int sub = 0; sub < Cfg::KSUB; ++sub) {
-            const float4* xr = reinterpret_cast<const float4*>(
-                sX + g * Cfg::XBUF_BYTES + sub * Cfg::TM * Cfg::XW + row_in_tile * Cfg::XW);
-#pragma unroll
-            for (int c = 0; c < Cfg::XW / 16; ++c) {
-              const float4 xv = xr[c];
-              n2 = fmaf(xv.x, xv.x, fmaf(xv.y, xv.y, fmaf(xv.z, xv.z, fmaf(xv.w, xv.w, n2))));
-            }
-          }
-          const float bound = sqrtf(n2) * fmax * 1.001f;
-          int ex = 0;
-          if (bound > 0.f) frexpf(bound, &ex);
-          er[g] = p.step ? 0 : 14 - ex;  // step values are 0 or 1: no scale needed
-        }
-        if (!ok) break;
-        // every epilogue warp has read its rows before any of them is rewritten
-        warp_arrive(x_rounded, lane);
-        if (!warp_wait(x_rounded, items_done & 1u, abort_flag, p.err, DEV_TIMEOUT_X,
-                       p.timeout_ns)) { ok = false; break; }
-        constexpr int UPR = Cfg::KSUB * Cfg::XW / 16;  // 16-byte units per row
-        for (int g = 0; g < w.ntiles; ++g) {
-          const float sc = __int_as_float((127 + er[g]) << 23);
-#pragma unroll
-          for (int u = half * (UPR / 2); u < (half + 1) * (UPR / 2); ++u) {
-            uint4* q = reinterpret_cast<uint4*>(sX + g * Cfg::XBUF_BYTES +
-                                                (u / (Cfg::XW / 16)) * Cfg::TM * Cfg::XW +
-                                                row_in_tile * Cfg::XW) + u % (Cfg::XW / 16);
+          for (int i = et; i < Cfg::TM * UPR; i += Cfg::EPI_THREADS) {
+            const int row = i / UPR, u = i % UPR;
+            uint4* q = reinterpret_cast<uint4*>(xt + (u / UPS) * Cfg::TM * Cfg::XW + row * Cfg::XW) +
+                       u % UPS;
             uint4 v = *q;
-            v.x = tf32_rne_bits(__float_as_uint(__uint_as_float(v.x) * sc));
-            v.y = tf32_rne_bits(__float_as_uint(__uint_as_float(v.y) * sc));
-            v.z = tf32_rne_bits(__float_as_uint(__uint_as_float(v.z) * sc));
-            v.w = tf32_rne_bits(__float_as_uint(__uint_as_float(v.w) * sc));
+            const float a = __uint_as_float(v.x), b = __uint_as_float(v.y);
+            const float c = __uint_as_float(v.z), d = __uint_as_float(v.w);
+            float n2 = fmaf(a, a, fmaf(b, b, fmaf(c, c, d * d)));
+#pragma unroll
+            for (int o = 1; o < UPR; o <<= 1) n2 += __shfl_xor_sync(0xffffffffu, n2, o);
+            // frexp exponent of the bound (zero: none); 2^er and 2^-er stay normal floats
+            const float bound = sqrtf(n2) * fmax * 1.001f;
+            const int ex = bound > 0.f ? ((__float_as_int(bound) >> 23) & 0xff) - 126 : 0;
+            const int e = p.step ? 0 : min(120, max(-120, 14 - ex));  // step values: 0 or 1
+            const float sc = __int_as_float((127 + e) << 23);
+            v.x = tf32_rne_bits(__float_as_uint(a * sc));
+            v.y = tf32_rne_bits(__float_as_uint(b * sc));
+            v.z = tf32_rne_bits(__float_as_uint(c * sc));
+            v.w = tf32_rne_bits(__float_as_uint(d * sc));
             *q = v;
+            if (u == 0) er_s[ers + row] = (int8_t)e;
           }
+        } else if constexpr (Cfg::ROUND) {
+          round_tf32_smem<Cfg::X_BYTES / 16, Cfg::EPI_THREADS>(xt, et);
         }
         fence_proxy_async_smem();
-        for (int g = 0; g < w.ntiles; ++g) warp_arrive(&x_ready[g], lane);
-      } else if constexpr (Cfg::ROUND) {
-        // round the group's X tiles to tf32 in place before the first MMA reads them
-        for (int gi = 0; gi < w.ntiles && ok; ++gi) {
-          if (!warp_wait(&x_full[gi], (slot_par >> gi) & 1u, abort_flag, p.err, DEV_TIMEOUT_X,
-                         p.timeout_ns)) { ok = false; break; }
-          round_tf32_smem<Cfg::X_BYTES / 16, Cfg::EPI_THREADS>(sX + gi * Cfg::XBUF_BYTES,
-                                                               threadIdx.x - 64);
-          fence_proxy_async_smem();
-          warp_arrive(&x_ready[gi], lane);
+        warp_arrive(&x_ready[xs], lane);
+        if (lane == 0 && warp == 2) SB_TR(24, li * G + g);
+        return true;
+      };
+      // Y readout of tile gi (product mode): scaled back, written to this split's partial rows
+      auto readout = [&](int gi) -> bool {
+        if constexpr (!REDUCE) {
+          if (!warp_wait(&y_full[gi], (slot_par >> gi) & 1u, abort_flag, p.err, DEV_TIMEOUT_Y,
+                         p.timeout_ns)) return false;
+          tc_fence_after();
+          if (warp == 2 && lane == 0) SB_TR(12, gi);
+          const int row = (w.tile0 + gi) * Cfg::TM + row_in_tile;
+          float inv = 1.f;
+          if constexpr (Cfg::ROW_SCALE) {
+            // the row's exponent, written by whichever thread prepared the row: every warp's
+            // x_ready arrival for the slot is complete by now (the wait orders the exponent's
+            // write before this read); the next group writes the other set
+            const int xs = xs0 + gi;
+            if (!warp_wait(&x_ready[xs], (xslot_par >> xs) & 1u, abort_flag, p.err, DEV_TIMEOUT_X,
+                           p.timeout_ns)) return false;
+            const int er = er_s[((li & 1) * G + gi) * Cfg::TM + row_in_tile];
+            inv = __int_as_float((127 - er - ec) << 23);
+          }
+          float* out = p.ws + ((size_t)split * p.M + (size_t)(row < p.M ? row : 0)) * DP;
+          // the two warps of a quadrant share the 16-column pieces of Y
+#pragma unroll 1
+          for (int col = half * 16; col < DP; col += 32) {
+            float y[16];
+            tmem_ld16(tbase + lane_addr + Cfg::TMEM_Y + gi * DP + col, y);
+            tmem_ld_wait_regs16(y);
+            if constexpr (Cfg::MS == 2) {
+              float y2[16];
+              tmem_ld16(tbase + lane_addr + Cfg::TMEM_Y + (G + gi) * DP + col, y2);
+              tmem_ld_wait_regs16(y2);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) y[i] += y2[i];
+            }
+            if (row < p.M) {
+              float4* o4 = reinterpret_cast<float4*>(out + col);
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                o4[i] = make_float4(y[4 * i] * inv, y[4 * i + 1] * inv, y[4 * i + 2] * inv,
+                                    y[4 * i + 3] * inv);
+            }
+          }
+          tc_fence_before();
+          warp_arrive(&y_empty[gi], lane);
+          if (warp == 2 && lane == 0) SB_TR(13, gi);
         }
-        if (!ok) break;
-      }
+        return true;
+      };
+      // In the first chunk the tiles are prepared XPRE_AHEAD pairs ahead of the pair being read
+      // (the first MMA starts on a tile as soon as it is ready, and the next tiles are prepared
+      // while it runs); in the last chunk each tile's Y is read out behind the next tile's pair,
+      // so that the readout overlaps the last MMAs.
+      constexpr int XPRE_AHEAD = 2;
+      int prepped = 0;
       for (int c = w.c0; c < w.c1 && ok; ++c) {
         for (int gi = 0; gi < w.ntiles; ++gi, ++pair) {
+          for (; prepped < w.ntiles && prepped <= gi + XPRE_AHEAD; ++prepped)
+            if (!prep_tile(prepped)) { ok = false; break; }
+          if (!ok) break;
           uint32_t buf, use;
           pair_slot<Cfg>(pair, buf, use);
           if (!warp_wait(&s_full[buf], use & 1, abort_flag, p.err, DEV_TIMEOUT_SFULL,
@@ -747,47 +818,13 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
           if (lane == 0 && warp == 2) SB_TR(5, pair);
           if (lane == 0 && warp == 9) SB_TR(6, pair);
           if (lane == 0) SB_TR(16 + warp - 2, pair);
+          if (c == w.c1 - 1 && gi > 0 && !readout(gi - 1)) { ok = false; break; }
         }
       }
       if (!ok) break;
-      if constexpr (!REDUCE) {
-        const int split = item % p.splits;
-        for (int gi = 0; gi < w.ntiles; ++gi) {
-          if (!warp_wait(&y_full[gi], (slot_par >> gi) & 1u, abort_flag, p.err, DEV_TIMEOUT_Y,
-                         p.timeout_ns)) { ok = false; break; }
-          tc_fence_after();
-          if (warp == 2 && lane == 0) SB_TR(12, gi);
-          const int row = (w.tile0 + gi) * Cfg::TM + row_in_tile;
-          const float inv = Cfg::H16 ? __int_as_float((127 - er[gi] - ec) << 23) : 1.f;
-          float* out = p.ws + ((size_t)split * p.M + (size_t)(row < p.M ? row : 0)) * DP;
-          // the two warps of a quadrant share the 16-column pieces of Y
-#pragma unroll 1
-          for (int col = half * 16; col < DP; col += 32) {
-            float y[16];
-            tmem_ld16(tbase + lane_addr + Cfg::TMEM_Y + gi * DP + col, y);
-            tmem_ld_wait_regs16(y);
-            if constexpr (Cfg::MS == 2) {
-              float y2[16];
-              tmem_ld16(tbase + lane_addr + Cfg::TMEM_Y + (G + gi) * DP + col, y2);
-              tmem_ld_wait_regs16(y2);
-#pragma unroll
-              for (int i = 0; i < 16; ++i) y[i] += y2[i];
-            }
-            if (row < p.M) {
-              float4* o4 = reinterpret_cast<float4*>(out + col);
-#pragma unroll
-              for (int i = 0; i < 4; ++i)
-                o4[i] = make_float4(y[4 * i] * inv, y[4 * i + 1] * inv, y[4 * i + 2] * inv,
-                                    y[4 * i + 3] * inv);
-            }
-          }
-          tc_fence_before();
-          warp_arrive(&y_empty[gi], lane);
-          if (warp == 2 && lane == 0) SB_TR(13, gi);
-        }
-      }
+      if (!readout(w.ntiles - 1)) { ok = false; break; }
       slot_par ^= (1u << w.ntiles) - 1u;
-      ++items_done;
+      xslot_par ^= ((1u << w.ntiles) - 1u) << xs0;
     }
     if constexpr (REDUCE) {
 #pragma unroll
@@ -815,8 +852,6 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
         if (p.count) p.partials[stride * blockIdx.x + 2] = c;
       }
     }
-    // wait (bounded) for this warp's own X copies still in flight before leaving
-    if (warp == 2 && *abort_flag && lane < G && xuses > 0) mbar_drain(&x_full[lane], (xuses - 1) & 1);
   } else if (Cfg::ROUND && warp == Cfg::CPREP_WARP) {
     if constexpr (Cfg::ROUND) {
     // ------------------------------------------------------------------ chunk prep (TF32 mode)
@@ -890,28 +925,45 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
       }
     }
     }
-  } else if (X3 && warp == 2 + Cfg::EPI_WARPS) {
-    // ------------------------------------------------------------------ X splitter (warp 10)
-    uint32_t slot_par = 0;
+  } else if (warp == Cfg::XLOAD_WARP) {
+    // ------------------------------------------------------------------ X loader
+    // Group k's tiles go to X slot set k % XB; lane g loads tile g as soon as the MMAs of the
+    // slot's previous group have completed (with two sets, while the previous group still runs)
+    uint32_t slot_par = 0;    // bit xs: parity of the number of earlier uses of X slot xs
+    uint32_t slot_used = 0;   // bit xs: slot used by an earlier group
+    uint32_t issued = 0, issued_par = 0;  // this lane's copies (drained on abort)
     bool ok = true;
-    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x) {
+    uint32_t li = 0;
+    for (int item = blockIdx.x; item < n_items && ok; item += gridDim.x, ++li) {
       const WorkItem w = work_item(p, item);
-      for (int gi = 0; gi < w.ntiles; ++gi) {
-        if (!warp_wait(&x_full[gi], (slot_par >> gi) & 1u, abort_flag, p.err, DEV_TIMEOUT_X,
-                       p.timeout_ns)) { ok = false; break; }
-        float4* xs = reinterpret_cast<float4*>(sX + gi * Cfg::XBUF_BYTES);
-        float4* xl = reinterpret_cast<float4*>(sX + gi * Cfg::XBUF_BYTES + Cfg::X_BYTES);
-        for (int i = lane; i < Cfg::X_BYTES / 16; i += 32) {
-          const float4 v = xs[i];
-          const float4 h = make_float4(tf32_hi(v.x), tf32_hi(v.y), tf32_hi(v.z), tf32_hi(v.w));
-          xs[i] = h;
-          xl[i] = make_float4(tf32_lo(v.x, h.x), tf32_lo(v.y, h.y), tf32_lo(v.z, h.z),
-                              tf32_lo(v.w, h.w));
+      const int xs0 = (int)(li % Cfg::XB) * G;
+      bool lok = true;
+      if (lane < w.ntiles) {
+        const int xs = xs0 + lane;
+        if ((slot_used >> xs) & 1u)
+          lok = mbar_wait(&x_empty[xs], ((slot_par >> xs) & 1u) ^ 1u, abort_flag, p.err,
+                          DEV_TIMEOUT_X, p.timeout_ns);
+        if (lok) {
+          uint8_t* xdst = sX + xs * Cfg::XBUF_BYTES;
+          mbar_arrive_expect_tx(&x_full[xs], Cfg::X_BYTES);
+#pragma unroll
+          for (int sub = 0; sub < Cfg::KSUB; ++sub)
+            tma_load_2d(xdst + sub * Cfg::TM * Cfg::XW, &tmX, sub * Cfg::BOX_K,
+                        (w.tile0 + lane) * Cfg::TM, &x_full[xs]);
+          issued |= 1u << xs;
+          issued_par = (issued_par & ~(1u << xs)) | (((slot_par >> xs) & 1u) << xs);
+          SB_TR(14, li * G + lane);
         }
-        fence_proxy_async_smem();
-        warp_arrive(&x_ready[gi], lane);
       }
-      slot_par ^= (1u << w.ntiles) - 1u;
+      if (!__all_sync(0xffffffffu, lok)) { ok = false; break; }
+      const uint32_t mask = ((1u << w.ntiles) - 1u) << xs0;
+      slot_par ^= mask;
+      slot_used |= mask;
+    }
+    if (*abort_flag) {
+      // wait (bounded) for this lane's copies still in flight before leaving
+      for (int xs = 0; xs < Cfg::NXS; ++xs)
+        if ((issued >> xs) & 1u) mbar_drain(&x_full[xs], (issued_par >> xs) & 1u);
     }
   }
 
