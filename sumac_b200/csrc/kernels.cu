@@ -782,146 +782,6 @@ __global__ void __launch_bounds__(256, 4) finalize_kernel(FinalizeArgs a) {
   }
 }
 
-// SALSA update with G^-1 at Dp = 16, one thread per row: the row's Y, X, dX, support term and
-// G^-1 product live in one thread's registers (G^-1 read from shared memory at one address per
-// warp: a broadcast), so no lane exchanges a value with another except for the rows with more
-// than FIN_ROW_K0 entries, whose remaining entries the whole warp shares (one entry per lane and
-// round, the 32 contributions summed by a butterfly). finalize_kernel's four lanes per row spend
-// most of their instructions on shuffles, masked rounds of four entries and 64-bit address
-// arithmetic (12 M issued warp instructions at C4: issue-bound, not HBM-bound).
-constexpr int FIN_ROW_K0 = 6;
-
-__global__ void __launch_bounds__(256, 2) finalize_salsa_rows_kernel(FinalizeArgs a) {
-  constexpr int DP = 16;
-  __shared__ __align__(16) float sg[DP * DP];
-  for (int i = threadIdx.x; i < DP * DP; i += blockDim.x) sg[i] = a.ginv[i];
-  __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const float mu = a.momentum, one_m_mu = 1.0f - mu;
-  const float lr = a.lrate, ub = *a.unbias;
-  const float4* ws4 = reinterpret_cast<const float4*>(a.ws);
-  float4* X4 = reinterpret_cast<float4*>(a.X);
-  float4* dX4 = reinterpret_cast<float4*>(a.dX);
-  const float4* F4 = reinterpret_cast<const float4*>(a.F);
-  const float4* C4 = reinterpret_cast<const float4*>(a.Cm);
-  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  // warp-uniform loop: the heavy-row rounds below need every lane
-  for (int64_t base = (int64_t)blockIdx.x * blockDim.x + (threadIdx.x & ~31); base < a.M;
-       base += stride) {
-    const int64_t j = base + lane;
-    const bool active = j < a.M;
-    const int64_t jr = active ? j : base;
-    float y[DP], x[DP], dx[DP], cor[DP];
-#pragma unroll
-    for (int v = 0; v < DP / 4; ++v) {
-      const float4 dv = dX4[jr * (DP / 4) + v];
-      float4 s = ws4[jr * (DP / 4) + v];
-      for (int q = 1; q < a.splits; ++q) {
-        const float4 t = ws4[((int64_t)q * a.M + jr) * (DP / 4) + v];
-        s.x += t.x; s.y += t.y; s.z += t.z; s.w += t.w;
-      }
-      const float4 xv = X4[jr * (DP / 4) + v];
-      dx[4 * v] = dv.x; dx[4 * v + 1] = dv.y; dx[4 * v + 2] = dv.z; dx[4 * v + 3] = dv.w;
-      y[4 * v] = s.x; y[4 * v + 1] = s.y; y[4 * v + 2] = s.z; y[4 * v + 3] = s.w;
-      x[4 * v] = xv.x; x[4 * v + 1] = xv.y; x[4 * v + 2] = xv.z; x[4 * v + 3] = xv.w;
-    }
-#pragma unroll
-    for (int k = 0; k < DP; ++k) cor[k] = 0.f;
-    const int e0 = active ? a.rowptr[j] : 0;
-    const int ne = active ? a.rowptr[j + 1] - e0 : 0;
-    // light part: the row's first FIN_ROW_K0 entries, in order
-    const int nl = ne < FIN_ROW_K0 ? ne : FIN_ROW_K0;
-    for (int q = 0; q < nl; ++q) {
-      const int2 en = a.ent[e0 + q];
-      float f[DP], c[DP];
-#pragma unroll
-      for (int v = 0; v < DP / 4; ++v) {
-        const float4 fv = F4[(int64_t)en.x * (DP / 4) + v];
-        const float4 cv = C4[(int64_t)en.x * (DP / 4) + v];
-        f[4 * v] = fv.x; f[4 * v + 1] = fv.y; f[4 * v + 2] = fv.z; f[4 * v + 3] = fv.w;
-        c[4 * v] = cv.x; c[4 * v + 1] = cv.y; c[4 * v + 2] = cv.z; c[4 * v + 3] = cv.w;
-      }
-      float L = 0.f;
-#pragma unroll
-      for (int k = 0; k < DP; ++k) L = fmaf(x[k], f[k], L);
-      const float coef = support_coef(FIN_SALSA, __int_as_float(en.y), L);
-#pragma unroll
-      for (int k = 0; k < DP; ++k) cor[k] = fmaf(coef, c[k], cor[k]);
-    }
-    // heavy part: the warp shares the rest of one row at a time
-    unsigned heavy = __ballot_sync(0xffffffffu, ne > FIN_ROW_K0);
-    while (heavy) {
-      const int src = __ffs(heavy) - 1;
-      heavy &= heavy - 1;
-      const int hb = __shfl_sync(0xffffffffu, e0, src) + FIN_ROW_K0;
-      const int hn = __shfl_sync(0xffffffffu, ne, src) - FIN_ROW_K0;
-      float hx[DP], part[DP];
-#pragma unroll
-      for (int k = 0; k < DP; ++k) {
-        hx[k] = __shfl_sync(0xffffffffu, x[k], src);
-        part[k] = 0.f;
-      }
-      for (int q = lane; q < hn; q += 32) {
-        const int2 en = a.ent[hb + q];
-        float f[DP], c[DP];
-#pragma unroll
-        for (int v = 0; v < DP / 4; ++v) {
-          const float4 fv = F4[(int64_t)en.x * (DP / 4) + v];
-          const float4 cv = C4[(int64_t)en.x * (DP / 4) + v];
-          f[4 * v] = fv.x; f[4 * v + 1] = fv.y; f[4 * v + 2] = fv.z; f[4 * v + 3] = fv.w;
-          c[4 * v] = cv.x; c[4 * v + 1] = cv.y; c[4 * v + 2] = cv.z; c[4 * v + 3] = cv.w;
-        }
-        float L = 0.f;
-#pragma unroll
-        for (int k = 0; k < DP; ++k) L = fmaf(hx[k], f[k], L);
-        const float coef = support_coef(FIN_SALSA, __int_as_float(en.y), L);
-#pragma unroll
-        for (int k = 0; k < DP; ++k) part[k] = fmaf(coef, c[k], part[k]);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-        for (int k = 0; k < DP; ++k) part[k] += __shfl_xor_sync(0xffffffffu, part[k], o);
-      }
-      if (lane == src) {
-#pragma unroll
-        for (int k = 0; k < DP; ++k) cor[k] += part[k];
-      }
-    }
-    if (!active) continue;
-    // u = (y - cor) G^{-1}
-    float u[DP];
-#pragma unroll
-    for (int k = 0; k < DP; ++k) u[k] = 0.f;
-#pragma unroll
-    for (int i = 0; i < DP; ++i) {
-      const float ti = y[i] - cor[i];
-#pragma unroll
-      for (int v = 0; v < DP / 4; ++v) {
-        const float4 g4 = reinterpret_cast<const float4*>(sg + i * DP)[v];
-        u[4 * v] = fmaf(ti, g4.x, u[4 * v]);
-        u[4 * v + 1] = fmaf(ti, g4.y, u[4 * v + 1]);
-        u[4 * v + 2] = fmaf(ti, g4.z, u[4 * v + 2]);
-        u[4 * v + 3] = fmaf(ti, g4.w, u[4 * v + 3]);
-      }
-    }
-    // lsq = x - u; dX' = (lsq - x)(1 - mu) + dX mu; X' = X + lr dX' / unbias (salsa.py:113-115)
-#pragma unroll
-    for (int v = 0; v < DP / 4; ++v) {
-      float nx[4], ndx[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int k = 4 * v + q;
-        const float lsq = x[k] - u[k];
-        ndx[q] = (lsq - x[k]) * one_m_mu + dx[k] * mu;
-        nx[q] = x[k] + lr * ndx[q] / ub;
-      }
-      X4[j * (DP / 4) + v] = make_float4(nx[0], nx[1], nx[2], nx[3]);
-      dX4[j * (DP / 4) + v] = make_float4(ndx[0], ndx[1], ndx[2], ndx[3]);
-    }
-  }
-}
-
 void launch_finalize(const FinalizeArgs& a, cudaStream_t stream) {
   if (a.M == 0) return;
   const int threads = 256;
@@ -929,10 +789,6 @@ void launch_finalize(const FinalizeArgs& a, cudaStream_t stream) {
   const unsigned grid = grid_cap(a.M * G, threads, 148 * 8);
   count_launch();
   if (a.ginv) {
-    if (a.Dp == 16 && a.mode == FIN_SALSA && a.rowptr) {
-      finalize_salsa_rows_kernel<<<grid_cap(a.M, 256, 148 * 2), 256, 0, stream>>>(a);
-      return;
-    }
     switch (a.Dp) {
       case 16: finalize_kernel<16, true><<<grid, threads, 0, stream>>>(a); break;
       case 32: finalize_kernel<32, true><<<grid, threads, 0, stream>>>(a); break;
