@@ -371,7 +371,7 @@ __global__ void __launch_bounds__(256) salsa_gather_kernel(
 }
 
 template <int D>
-__global__ void __launch_bounds__(256) salsa_ginv_kernel(
+__global__ void __launch_bounds__(64) salsa_ginv_kernel(
     const float* __restrict__ FI, int64_t b, int d, int Dp, double* __restrict__ parts,
     unsigned int* counter, double* __restrict__ LU, int* __restrict__ piv,
     float* __restrict__ ginv, int* err) {
@@ -461,11 +461,14 @@ void launch_salsa_ginv(const float* FI, int64_t b, int d, int Dp, void* scratch,
   double* parts = reinterpret_cast<double*>(scratch);
   double* LU = parts + (size_t)np * d * d;
   int* piv = reinterpret_cast<int*>(LU + 32 * 32);
+  // 64 threads: the kernel runs on a side stream beside the fused product, whose CTA holds ~54 k
+  // of an SM's 64 k registers; a 256-thread CTA (96 registers each) could not share an SM with
+  // it and kept 22 product CTAs waiting for its ~20 us (measured: ~20 us per update)
   count_launch();
   if (Dp == 16)
-    salsa_ginv_kernel<16><<<np, 256, 0, stream>>>(FI, b, d, Dp, parts, counter, LU, piv, ginv, err);
+    salsa_ginv_kernel<16><<<np, 64, 0, stream>>>(FI, b, d, Dp, parts, counter, LU, piv, ginv, err);
   else
-    salsa_ginv_kernel<32><<<np, 256, 0, stream>>>(FI, b, d, Dp, parts, counter, LU, piv, ginv, err);
+    salsa_ginv_kernel<32><<<np, 64, 0, stream>>>(FI, b, d, Dp, parts, counter, LU, piv, ginv, err);
 }
 
 // ============================================================================================
