@@ -399,12 +399,15 @@ int sumac_salsa_block_update(const float* F, int64_t m_fixed, const int64_t* row
     cudaStreamWaitEvent(side->stream, side->fork, 0);
     launch_salsa_ginv(p.FI, b, d, Dp, p.gram, p.counter, p.ginv, dev_err, side->stream);
     cudaEventRecord(side->join, side->stream);
+    // the product leaves kGinvSms SMs to the Gram-inverse launch, which then runs at full speed
+    // instead of sharing issue slots with product CTAs
+    const int psms = sms > 2 * kGinvSms ? sms - kGinvSms : sms;
     int rc = launch_relu_product(X, M, p.Fhi, p.Flo, p.Cthi, p.Ctlo, p.ldct, b, Dp,
-                                 x3, p.part, dev_err, sms, g_timeout_ns, s, p.counter + 1, 0, 1);
+                                 x3, p.part, dev_err, psms, g_timeout_ns, s, p.counter + 1, 0, 1);
     cudaStreamWaitEvent(s, side->join, 0);
     if (rc) return cuda_status(rc, "salsa_block_update");
     FinalizeArgs f{};
-    f.mode = FIN_SALSA; f.M = M; f.Dp = Dp; f.splits = product_split_count(M, b, Dp, x3, sms);
+    f.mode = FIN_SALSA; f.M = M; f.Dp = Dp; f.splits = product_split_count(M, b, Dp, x3, psms);
     f.ws = p.part; f.X = X; f.dX = dX; f.F = p.FI; f.Cm = p.FI; f.ginv = p.ginv;
     f.rowptr = rowptr; f.ent = reinterpret_cast<const int2*>(ent);
     f.momentum = momentum; f.lrate = lrate; f.unbias = unbias;

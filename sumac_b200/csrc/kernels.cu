@@ -4,6 +4,8 @@
 #include <atomic>
 #include <cstdint>
 
+#include <algorithm>
+
 #include "kernels.cuh"
 #include "sm100.cuh"
 
@@ -371,27 +373,49 @@ __global__ void __launch_bounds__(256) salsa_gather_kernel(
 }
 
 template <int D>
-__global__ void __launch_bounds__(64) salsa_ginv_kernel(
-    const float* __restrict__ FI, int64_t b, int d, int Dp, double* __restrict__ parts,
-    unsigned int* counter, double* __restrict__ LU, int* __restrict__ piv,
-    float* __restrict__ ginv, int* err) {
+__global__ void __launch_bounds__(256) salsa_ginv_kernel(
+    const float* __restrict__ FI, int64_t b, int d, int Dp, int64_t rows_per_cta,
+    double* __restrict__ parts, unsigned int* counter, double* __restrict__ LU,
+    int* __restrict__ piv, float* __restrict__ ginv, int* err) {
   __shared__ float srow[PREP_ROWS * (D + 1)];
   __shared__ double sG[D * D];
   __shared__ bool last;
-  const int64_t r0 = (int64_t)blockIdx.x * PREP_ROWS;
-  const int nr = (int)min((int64_t)PREP_ROWS, b - r0);
-  for (int i = threadIdx.x; i < nr * D; i += blockDim.x) {
-    const int rr = i / D, c = i - rr * D;
-    srow[rr * (D + 1) + c] = c < d ? FI[(r0 + rr) * Dp + c] : 0.f;
-  }
-  __syncthreads();
   const int dd = d * d;
-  for (int e = threadIdx.x; e < dd; e += blockDim.x) {
-    const int i = e / d, j = e - i * d;
-    double s = 0.0;
-    for (int rr = 0; rr < nr; ++rr)
-      s += (double)srow[rr * (D + 1) + i] * (double)srow[rr * (D + 1) + j];
-    parts[(size_t)blockIdx.x * dd + e] = s;
+  // this CTA's rows [r0, r1), staged PREP_ROWS at a time; each thread keeps its entries' sums
+  constexpr int EPT = (D * D + 255) / 256;  // Gram entries per thread
+  double acc[EPT];
+#pragma unroll
+  for (int q = 0; q < EPT; ++q) acc[q] = 0.0;
+  const int64_t r0 = (int64_t)blockIdx.x * rows_per_cta;
+  const int64_t r1 = min(b, r0 + rows_per_cta);
+  for (int64_t c0 = r0; c0 < r1; c0 += PREP_ROWS) {
+    const int nr = (int)min((int64_t)PREP_ROWS, r1 - c0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nr * D; i += blockDim.x) {
+      const int rr = i / D, c = i - rr * D;
+      srow[rr * (D + 1) + c] = c < d ? FI[(c0 + rr) * Dp + c] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < EPT; ++q) {
+      const int e = threadIdx.x + q * 256;
+      if (e < dd) {
+        const int i = e / d, j = e - i * d;
+        double s0 = 0.0, s1 = 0.0;
+        int rr = 0;
+        for (; rr + 1 < nr; rr += 2) {
+          s0 += (double)srow[rr * (D + 1) + i] * (double)srow[rr * (D + 1) + j];
+          s1 += (double)srow[(rr + 1) * (D + 1) + i] * (double)srow[(rr + 1) * (D + 1) + j];
+        }
+        if (rr < nr) s0 += (double)srow[rr * (D + 1) + i] * (double)srow[rr * (D + 1) + j];
+        acc[q] += s0 + s1;
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < EPT; ++q) {
+    const int e = threadIdx.x + q * 256;
+    if (e < dd) parts[(size_t)blockIdx.x * dd + e] = acc[q];
   }
   __threadfence();
   __syncthreads();
@@ -457,18 +481,20 @@ void launch_salsa_gather(const float* Ffix, const int64_t* rows, int64_t b, int 
 
 void launch_salsa_ginv(const float* FI, int64_t b, int d, int Dp, void* scratch,
                        unsigned int* counter, float* ginv, int* err, cudaStream_t stream) {
-  const int np = salsa_gram_parts(b);
+  // at most kGinvSms CTAs (one per SM: a 256-thread CTA cannot share an SM with a product CTA),
+  // on the SMs the concurrent fused product leaves free
+  const int64_t rpc = std::max<int64_t>(PREP_ROWS, cdiv64(b > 0 ? b : 1, kGinvSms));
+  const int np = (int)cdiv64(b > 0 ? b : 1, rpc);
   double* parts = reinterpret_cast<double*>(scratch);
-  double* LU = parts + (size_t)np * d * d;
+  double* LU = parts + (size_t)salsa_gram_parts(b) * d * d;
   int* piv = reinterpret_cast<int*>(LU + 32 * 32);
-  // 64 threads: the kernel runs on a side stream beside the fused product, whose CTA holds ~54 k
-  // of an SM's 64 k registers; a 256-thread CTA (96 registers each) could not share an SM with
-  // it and kept 22 product CTAs waiting for its ~20 us (measured: ~20 us per update)
   count_launch();
   if (Dp == 16)
-    salsa_ginv_kernel<16><<<np, 64, 0, stream>>>(FI, b, d, Dp, parts, counter, LU, piv, ginv, err);
+    salsa_ginv_kernel<16><<<np, 256, 0, stream>>>(FI, b, d, Dp, rpc, parts, counter, LU, piv,
+                                                  ginv, err);
   else
-    salsa_ginv_kernel<32><<<np, 64, 0, stream>>>(FI, b, d, Dp, parts, counter, LU, piv, ginv, err);
+    salsa_ginv_kernel<32><<<np, 256, 0, stream>>>(FI, b, d, Dp, rpc, parts, counter, LU, piv,
+                                                  ginv, err);
 }
 
 // ============================================================================================

@@ -61,6 +61,8 @@ int salsa_gram_parts(int64_t b);
 // transpose C^T = F_I^T split in 3xTF32 mode, and the operand maxima into stats[0..1], zero
 // before) in one launch; then G^{-1} of G = F_I^T F_I into ginv [Dp][Dp] (fp32) in one launch whose
 // last CTA factors G. scratch: salsa_ginv_scratch_bytes(b, d); counter zero before the first use.
+// SMs the Gram-inverse launch uses beside the fused product, which then runs on num_sms - kGinvSms
+constexpr int kGinvSms = 11;
 size_t salsa_ginv_scratch_bytes(int64_t b, int d);
 void launch_salsa_gather(const float* Ffix, const int64_t* rows, int64_t b, int Dp, float* FI,
                          float* Fhi, float* Flo, float* Cthi, float* Ctlo, int64_t ldct,
