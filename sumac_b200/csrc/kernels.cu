@@ -253,58 +253,6 @@ static constexpr int PREP_ROWS = 64;
 
 int salsa_gram_parts(int64_t b) { return cdiv64(b, PREP_ROWS) < 1 ? 1 : cdiv64(b, PREP_ROWS); }
 
-// Register LU with partial pivoting of the D x D matrix G (padded with an identity block),
-// by one warp: lane i keeps row i of G in registers for the whole factorisation; the row
-// exchanges of getrf are tracked as a permutation instead of being moved between lanes. Writes
-// the packed L\U factors in pivoted row order and getrf's pivot sequence (at step k the first
-// row, in the current exchanged order, of maximal |a_k| wins).
-template <int D>
-__device__ __forceinline__ void warp_lu(const double* __restrict__ G, int d, double* LU, int* piv,
-                                        int* err) {
-  static_assert(D <= 32, "one row per lane");
-  const int lane = threadIdx.x & 31;
-  double a[D];
-#pragma unroll
-  for (int j = 0; j < D; ++j)
-    a[j] = (lane < d && j < d) ? G[lane * d + j] : (lane == j ? 1.0 : 0.0);
-  int pos = lane;       // this lane's row position in the exchanged order
-  bool done = lane >= D;  // row already used as a pivot (or not a row)
-#pragma unroll
-  for (int k = 0; k < D; ++k) {
-    // the largest |a_k| among the remaining rows: compare the bit patterns of the non-negative
-    // doubles (monotonic), high word first; ties go to the smallest exchanged position
-    const unsigned long long key =
-        done ? 0ull : (unsigned long long)__double_as_longlong(fabs(a[k]));
-    const unsigned hi = (unsigned)(key >> 32), lo = (unsigned)key;
-    const unsigned mhi = __reduce_max_sync(0xffffffffu, done ? 0u : hi);
-    const bool c1 = !done && hi == mhi;
-    const unsigned mlo = __reduce_max_sync(0xffffffffu, c1 ? lo : 0u);
-    const bool c2 = c1 && lo == mlo;
-    const unsigned mpos = __reduce_min_sync(0xffffffffu, c2 ? (unsigned)pos : 0xffffffffu);
-    const bool me = c2 && (unsigned)pos == mpos;
-    const int src = __ffs(__ballot_sync(0xffffffffu, me)) - 1;  // lane holding the pivot row
-    // getrf exchanges positions k and mpos: the row at position k moves to mpos
-    if (lane == 0) {
-      piv[k] = (int)mpos;
-      if (mhi == 0u && mlo == 0u && err) atomicCAS(err, 0, DEV_SINGULAR);
-    }
-    if (!done && pos == k) pos = (int)mpos;
-    if (me) { pos = k; done = true; }
-    double u[D];
-#pragma unroll
-    for (int j = k; j < D; ++j) u[j] = __shfl_sync(0xffffffffu, a[j], src);
-    if (!done) {
-      const double l = a[k] / u[k];
-      a[k] = l;
-#pragma unroll
-      for (int j = k + 1; j < D; ++j) a[j] -= l * u[j];
-    }
-  }
-  if (lane < D) {
-#pragma unroll
-    for (int j = 0; j < D; ++j) LU[pos * D + j] = a[j];
-  }
-}
 
 // ============================================================================================
 // SALSA block step without the least-squares map P (training/salsa.py:138-140 rewritten):
@@ -314,9 +262,10 @@ __device__ __forceinline__ void warp_lu(const double* __restrict__ G, int d, dou
 // are needed only by the finalize pass: they are computed on a side stream while the product runs.
 //   salsa_gather_kernel  F_I = F[rows] (fp32, tf32 hi / lo halves), C^T = F_I^T (split in 3xTF32
 //                        mode) and the operand maxima of the TF32 product, 32 rows per CTA
-//   salsa_ginv_kernel    partial Gram per 64 rows (fp64); the last CTA sums the partials in a fixed
-//                        order, factors G (warp_lu: LAPACK getrf's pivot choice) and writes
-//                        G^{-1} [Dp][Dp] (fp32, zero outside d x d) column by column
+//   salsa_ginv_kernel    partial Grams (fp64) of the block rows split over at most kGinvSms CTAs;
+//                        the last CTA sums them in CTA order and inverts G by Gauss-Jordan
+//                        elimination (getrf's pivot choice): G^{-1} [Dp][Dp] (fp32, zero
+//                        outside d x d)
 // ============================================================================================
 __global__ void __launch_bounds__(256) salsa_gather_kernel(
     const float* __restrict__ Ffix, const int64_t* __restrict__ rows, int64_t b, int Dp,
@@ -378,7 +327,8 @@ __global__ void __launch_bounds__(256) salsa_ginv_kernel(
     double* __restrict__ parts, unsigned int* counter, double* __restrict__ LU,
     int* __restrict__ piv, float* __restrict__ ginv, int* err) {
   __shared__ float srow[PREP_ROWS * (D + 1)];
-  __shared__ double sG[D * D];
+  __shared__ double aug[2][D][2 * D];  // [G | I] and its Gauss-Jordan iterates (double-buffered)
+  __shared__ int s_piv;
   __shared__ bool last;
   const int dd = d * d;
   // this CTA's rows [r0, r1), staged PREP_ROWS at a time; each thread keeps its entries' sums
@@ -423,44 +373,65 @@ __global__ void __launch_bounds__(256) salsa_ginv_kernel(
   __syncthreads();
   if (!last) return;
   __threadfence();
-  for (int e = threadIdx.x; e < dd; e += blockDim.x) {
-    double s = 0.0;
+  for (int e = threadIdx.x; e < D * 2 * D; e += blockDim.x) {
+    const int i = e / (2 * D), j = e - i * (2 * D);
+    double v = 0.0;
+    if (j < D) {
+      if (i < d && j < d) {
 #pragma unroll 8
-    for (int q = 0; q < (int)gridDim.x; ++q) s += __ldcg(&parts[(size_t)q * dd + e]);
-    sG[e] = s;
+        for (int q = 0; q < (int)gridDim.x; ++q) v += __ldcg(&parts[(size_t)q * dd + i * d + j]);
+      }
+    } else {
+      v = (j - D == i) ? 1.0 : 0.0;
+    }
+    aug[0][i][j] = v;
   }
   __syncthreads();
-  if (threadIdx.x < 32) warp_lu<D>(sG, d, LU, piv, err);
-  __threadfence_block();
-  __syncthreads();
-  // column c of G^{-1}: solve P L U x = e_c (exchanges applied as getrf recorded them)
-  if ((int)threadIdx.x < Dp) {
-    const int c = threadIdx.x;
-    double x[D];
+  // G^{-1} by Gauss-Jordan elimination of [G | I] with partial pivoting (at step k the row, at or
+  // below k, of largest |entry| in column k, the first on ties: getrf's pivot choice). Every
+  // thread updates its elements of the augmented matrix from the previous iterate; two barriers
+  // per step. Rows and columns beyond d stay the identity.
+  (void)LU;
+  (void)piv;
+  for (int k = 0; k < d; ++k) {
+    double(*cur)[2 * D] = aug[k & 1];
+    double(*nxt)[2 * D] = aug[(k + 1) & 1];
+    if (threadIdx.x < 32) {
+      const int i = threadIdx.x;
+      double v = (i >= k && i < d) ? fabs(cur[i][k]) : -1.0;
+      int idx = i;
 #pragma unroll
-    for (int k = 0; k < D; ++k) x[k] = (k == c && c < d) ? 1.0 : 0.0;
-#pragma unroll
-    for (int k = 0; k < D; ++k) {
-      const int pk = piv[k];
-#pragma unroll
-      for (int j = k + 1; j < D; ++j)
-        if (j == pk) { const double tv = x[k]; x[k] = x[j]; x[j] = tv; }
+      for (int o = 16; o > 0; o >>= 1) {
+        const double ov = __shfl_xor_sync(0xffffffffu, v, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+        if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
+      }
+      if (i == 0) {
+        s_piv = idx;
+        if (v == 0.0 && err) atomicCAS(err, 0, DEV_SINGULAR);
+      }
     }
-#pragma unroll
-    for (int i = 1; i < D; ++i) {
-      double s = x[i];
-#pragma unroll
-      for (int j = 0; j < i; ++j) s -= LU[i * D + j] * x[j];
-      x[i] = s;
+    __syncthreads();
+    const int pr = s_piv;
+    const double inv = 1.0 / cur[pr][k];
+    for (int e = threadIdx.x; e < D * 2 * D; e += blockDim.x) {
+      const int i = e / (2 * D), j = e - i * (2 * D);
+      const double rowk = cur[pr][j] * inv;  // the pivot row, moved to k and scaled
+      if (i == k) {
+        nxt[i][j] = rowk;
+      } else {
+        const int src = i == pr ? k : i;      // row pr takes the old row k
+        nxt[i][j] = cur[src][j] - cur[src][k] * rowk;
+      }
     }
-#pragma unroll
-    for (int i = D - 1; i >= 0; --i) {
-      double s = x[i];
-#pragma unroll
-      for (int j = i + 1; j < D; ++j) s -= LU[i * D + j] * x[j];
-      x[i] = s / LU[i * D + i];
+    __syncthreads();
+  }
+  {
+    double(*fin)[2 * D] = aug[d & 1];
+    for (int e = threadIdx.x; e < Dp * Dp; e += blockDim.x) {
+      const int k = e / Dp, c = e - k * Dp;
+      ginv[e] = (k < d && c < d) ? (float)fin[k][D + c] : 0.f;
     }
-    for (int k = 0; k < Dp; ++k) ginv[k * Dp + c] = (k < d && c < d) ? (float)x[k] : 0.f;
   }
   if (threadIdx.x == 0) *counter = 0u;  // ready for the next launch (graph replays included)
 }
