@@ -205,6 +205,23 @@ int sumac_sgd_step(float* p, float* g, float* buf, int64_t n, float lr, float mo
 int sumac_fill_zero(float* p, int64_t n, sumac_stream_t stream);
 
 /*
+ * Row exchange of the row-sharded multi-GPU SALSA step over NVLink peer memory (no counterpart
+ * kernel in the reference, which moves whole factors between devices, training/salsa.py:169-209).
+ * peer_bufs: device array [world] of every rank's exchange buffer (two slots of slot_floats floats);
+ * peer_flags: device array [world] of every rank's flag array (world unsigned ints, zero at start);
+ * epoch: this rank's exchange counter on the device (zero at start). The call stores the rows
+ * rows[p] that this rank owns (lo <= rows[p] < hi, local = its rows [lo, hi)) into row p of slot
+ * (epoch + 1) & 1 of every rank's buffer, signals every rank and waits for every rank's signal
+ * (bounded; a timeout writes code 8 into dev_err). Every rank must make the same
+ * sequence of calls; between two calls that use the same slot, the readers of that slot must have
+ * been enqueued on `stream` before the intervening call.
+ */
+int sumac_assemble_rows_p2p(const float* local, int64_t lo, int64_t hi, const int64_t* rows,
+                            int64_t nrows, int Dp, int64_t slot_floats, float* const* peer_bufs,
+                            unsigned int* const* peer_flags, unsigned int* epoch, int rank,
+                            int world, int* dev_err, sumac_stream_t stream);
+
+/*
  * Initial SALSA factors (replaces the sparse products and the gathered dot products of
  * init_salsa_factors, src/sumac/training/salsa.py:36-78).
  * sumac_init_factor: out[r][c] = sign * sqrt(sum_{e in [rowptr[r], rowptr[r+1])} val[e] R[col[e]][c])

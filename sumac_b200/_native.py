@@ -63,6 +63,7 @@ _SIGS = {
     "sumac_grad_sumsq": (i32, [p, i64, p, p]),
     "sumac_sgd_step": (i32, [p, p, p, i64, f32, f32, i32, p, f32, p]),
     "sumac_fill_zero": (i32, [p, i64, p]),
+    "sumac_assemble_rows_p2p": (i32, [p, i64, i64, p, i64, i32, i64, p, p, p, i32, i32, p, p]),
     "sumac_init_factor": (i32, [p, p, p, i64, p, i32, f32, p, p]),
     "sumac_init_scale_workspace_bytes": (sz, []),
     "sumac_init_scale_terms": (i32, [p, p, i32, p, p, p, i64, p, p, sz, p]),
@@ -142,6 +143,7 @@ DEVICE_ERRORS = {
     5: "the output accumulator wait timed out",
     6: "the row-tile load wait timed out",
     7: "flag wait timed out",
+    8: "a peer GPU did not signal the row exchange in time",
     100: "singular Gram matrix in the SALSA least-squares solve",
 }
 

@@ -701,6 +701,21 @@ int sumac_gather_owned_rows(const float* local, int64_t lo, int64_t hi, const in
   return launched("gather_owned_rows");
 }
 
+int sumac_assemble_rows_p2p(const float* local, int64_t lo, int64_t hi, const int64_t* rows,
+                            int64_t nrows, int Dp, int64_t slot_floats, float* const* peer_bufs,
+                            unsigned int* const* peer_flags, unsigned int* epoch, int rank,
+                            int world, int* dev_err, sumac_stream_t stream) {
+  if (nrows < 0 || hi < lo || padded(Dp) != Dp || world < 1 || world > 512 || rank < 0 ||
+      rank >= world || !peer_bufs || !peer_flags || !epoch || slot_floats < nrows * Dp ||
+      (nrows > 0 && !rows) || (nrows > 0 && hi > lo && !local))
+    return fail(SUMAC_ERR_ARG, "assemble_rows_p2p: bad args");
+  if (!aligned16(local)) return fail(SUMAC_ERR_ARG, "assemble_rows_p2p: rows must be 16-byte aligned");
+  launch_assemble_rows_p2p(local, lo, hi, rows, nrows, Dp, slot_floats, peer_bufs, peer_flags,
+                           epoch, rank, world, dev_err, g_timeout_ns,
+                           reinterpret_cast<cudaStream_t>(stream));
+  return launched("assemble_rows_p2p");
+}
+
 int sumac_fill_zero(float* p, int64_t n, sumac_stream_t stream) {
   if (n < 0 || (n > 0 && !p)) return fail(SUMAC_ERR_ARG, "fill_zero: bad args");
   launch_fill_zero(p, n, reinterpret_cast<cudaStream_t>(stream));

@@ -1580,6 +1580,68 @@ __global__ void gather_owned_rows_kernel(const float* __restrict__ local, int64_
   }
 }
 
+// Row exchange of the row-sharded SALSA step over NVLink peer memory: every rank stores the block
+// rows it owns (rows[p] in [lo, hi)) into slot (epoch & 1) of every rank's buffer (itself
+// included; each row has exactly one owner, so the slot is complete once all ranks have written),
+// then sets its flag in every rank's flag array to the new epoch (release, system scope) and waits
+// (acquire, bounded) until every rank's flag in its own array has reached it. One CTA. Slot reuse:
+// a peer writes slot s for exchange e only after passing exchange e - 1, for which this rank
+// signalled only once everything it had enqueued before exchange e - 1 (the readers of slot s from
+// exchange e - 2) had completed.
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(512) assemble_rows_p2p_kernel(
+    const float* __restrict__ local, int64_t lo, int64_t hi, const int64_t* __restrict__ rows,
+    int64_t nrows, int Dp, int64_t slot_floats, float* const* __restrict__ peer_bufs,
+    unsigned* const* __restrict__ peer_flags, unsigned* epoch, int rank, int world, int* err,
+    unsigned long long timeout_ns) {
+  const unsigned ep = *epoch + 1u;
+  const int64_t slot_off = (int64_t)(ep & 1u) * slot_floats;
+  const int v4 = Dp / 4;
+  for (int64_t e = threadIdx.x; e < nrows * v4; e += blockDim.x) {
+    const int64_t p = e / v4;
+    const int v = (int)(e - p * v4);
+    const int64_t g = rows[p];
+    if (g >= lo && g < hi) {
+      const float4 val = reinterpret_cast<const float4*>(local)[(g - lo) * v4 + v];
+      for (int q = 0; q < world; ++q)
+        reinterpret_cast<float4*>(peer_bufs[q] + slot_off)[p * v4 + v] = val;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if ((int)threadIdx.x < world) {
+    st_release_sys(peer_flags[threadIdx.x] + rank, ep);
+    const unsigned* mine = peer_flags[rank] + threadIdx.x;
+    const uint64_t t0 = globaltimer_ns();
+    while ((int)(ld_acquire_sys(mine) - ep) < 0) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        if (err) atomicCAS(err, 0, DEV_TIMEOUT_PEER);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *epoch = ep;
+}
+
+void launch_assemble_rows_p2p(const float* local, int64_t lo, int64_t hi, const int64_t* rows,
+                              int64_t nrows, int Dp, int64_t slot_floats, float* const* peer_bufs,
+                              unsigned* const* peer_flags, unsigned* epoch, int rank, int world,
+                              int* err, unsigned long long timeout_ns, cudaStream_t stream) {
+  count_launch();
+  assemble_rows_p2p_kernel<<<1, 512, 0, stream>>>(local, lo, hi, rows, nrows, Dp, slot_floats,
+                                                   peer_bufs, peer_flags, epoch, rank, world, err,
+                                                   timeout_ns);
+}
+
 void launch_gather_owned_rows(const float* local, int64_t lo, int64_t hi, const int64_t* rows,
                               int64_t nrows, int Dp, float* out, cudaStream_t stream) {
   if (nrows <= 0) return;

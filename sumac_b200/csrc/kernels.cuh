@@ -70,6 +70,12 @@ void launch_salsa_gather(const float* Ffix, const int64_t* rows, int64_t b, int 
 void launch_salsa_ginv(const float* FI, int64_t b, int d, int Dp, void* scratch,
                        unsigned int* counter, float* ginv, int* err, cudaStream_t stream);
 
+// Row exchange over NVLink peer memory (see kernels.cu): the owned rows of rows[0..nrows) into
+// slot (epoch & 1) of every rank's buffer, then a flag barrier with a bounded wait.
+void launch_assemble_rows_p2p(const float* local, int64_t lo, int64_t hi, const int64_t* rows,
+                              int64_t nrows, int Dp, int64_t slot_floats, float* const* peer_bufs,
+                              unsigned* const* peer_flags, unsigned* epoch, int rank, int world,
+                              int* err, unsigned long long timeout_ns, cudaStream_t stream);
 // out[p] = local[rows[p] - lo] if lo <= rows[p] < hi else 0 (Dp floats per row).
 void launch_gather_owned_rows(const float* local, int64_t lo, int64_t hi, const int64_t* rows,
                               int64_t nrows, int Dp, float* out, cudaStream_t stream);

@@ -17,6 +17,7 @@ enum : int {
   DEV_TIMEOUT_Y = 5,         // wait on the output accumulator
   DEV_TIMEOUT_X = 6,         // wait on the row-tile load / conversion
   DEV_TIMEOUT_FLAG = 7,      // bounded wait on a host-controlled flag (test hook)
+  DEV_TIMEOUT_PEER = 8,      // a peer GPU did not signal the row exchange in time
   DEV_SINGULAR = 100,        // exactly singular Gram matrix in the SALSA solve
 };
 

@@ -243,3 +243,15 @@ def init_scale_terms(A, B, ei, ej, v):
     check(L.sumac_init_scale_terms(ptr(A), ptr(B), A.shape[1], ptr(ei), ptr(ej), ptr(v), v.numel(),
                                    ptr(out), ptr(ws), nb, N.stream_ptr(A.device)), "init_scale_terms")
     return out
+
+
+def assemble_rows_p2p(local, lo, hi, rows, nrows, slot_floats, peer_bufs, peer_flags, epoch,
+                      rank, world):
+    """Row exchange over NVLink peer memory (sumac_assemble_rows_p2p): this rank's rows of
+    rows[:nrows] into slot (epoch + 1) & 1 of every rank's buffer, then a flag barrier."""
+    dev = epoch.device
+    check(N.lib().sumac_assemble_rows_p2p(ptr(local), int(lo), int(hi), ptr(rows), int(nrows),
+                                          local.shape[1], int(slot_floats), ptr(peer_bufs),
+                                          ptr(peer_flags), ptr(epoch), int(rank), int(world),
+                                          ptr(N.err_word(dev)), N.stream_ptr(dev)),
+          "assemble_rows_p2p")

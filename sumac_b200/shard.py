@@ -59,6 +59,70 @@ class SymmetricRows:
         torch.ops.symm_mem.one_shot_all_reduce_out(self.buf[:b], "sum", self.group_name, out)
 
 
+class P2PRows:
+    """Block-row exchange over NVLink peer memory: a two-slot [2, rows, Dp] buffer and a flag
+    array in symmetric memory on every rank, and a device exchange counter. Each exchange
+    (`assemble`) is one native kernel: this rank stores the rows it owns into the current slot of
+    every rank's buffer, then a flag barrier (one round, bounded wait) -- against the two barrier
+    rounds and the reduction of a one-shot allreduce. Every rank makes the same sequence of calls;
+    `pad_even` keeps the number of calls per iteration even, so that the slots a captured CUDA
+    graph bakes in stay right on every replay."""
+
+    def __init__(self, rows: int, Dp: int, device, group=None):
+        import torch.distributed._symmetric_memory as symm_mem
+        g = group or dist.group.WORLD
+        name = g.group_name
+        self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        self.rows, self.Dp = rows, Dp
+        self.buf = symm_mem.empty((2, rows, Dp), dtype=torch.float32, device=device)
+        hb = symm_mem.rendezvous(self.buf, name)
+        self.flags = symm_mem.empty((self.world,), dtype=torch.int32, device=device)
+        hf = symm_mem.rendezvous(self.flags, name)
+        self.flags.zero_()
+        self.buf.zero_()
+        ob = self.buf.data_ptr() - hb.buffer_ptrs[self.rank]
+        of = self.flags.data_ptr() - hf.buffer_ptrs[self.rank]
+        self.peer_bufs = torch.tensor([p + ob for p in hb.buffer_ptrs], dtype=torch.int64,
+                                      device=device)
+        self.peer_flags = torch.tensor([p + of for p in hf.buffer_ptrs], dtype=torch.int64,
+                                       device=device)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        self.calls = 0
+        self.empty_rows = torch.zeros(1, dtype=torch.int64, device=device)
+        torch.cuda.synchronize(device)
+        dist.barrier(group=group)  # every rank's flags are zero before anyone signals
+
+    def assemble(self, local: Tensor, lo: int, hi: int, rows: Tensor) -> Tensor:
+        """F[rows] (the assembled block rows) on every rank, as a view of the current slot."""
+        b = rows.numel()
+        self.calls += 1
+        ops.assemble_rows_p2p(local, lo, hi, rows, b, self.rows * self.Dp, self.peer_bufs,
+                              self.peer_flags, self.epoch, self.rank, self.world)
+        return self.buf[self.calls & 1, :b]
+
+    def pad_even(self, local: Tensor) -> None:
+        if self.calls & 1:
+            self.calls += 1
+            ops.assemble_rows_p2p(local, 0, 0, self.empty_rows, 0, self.rows * self.Dp,
+                                  self.peer_bufs, self.peer_flags, self.epoch, self.rank,
+                                  self.world)
+
+
+def make_p2p_rows(rows: int, Dp: int, device, group=None):
+    """P2PRows on CUDA when symmetric memory is available, else None."""
+    if device.type != "cuda":
+        return None
+    # ranks spinning on each other's flags must each have a GPU of their own
+    ids = [None] * dist.get_world_size(group)
+    dist.all_gather_object(ids, str(torch.cuda.get_device_properties(device).uuid), group=group)
+    if len(set(ids)) != len(ids):
+        return None
+    try:
+        return P2PRows(rows, Dp, device, group)
+    except Exception:  # no peer access or no symmetric-memory backend
+        return None
+
+
 def make_symmetric_rows(rows: int, Dp: int, device, group=None):
     """SymmetricRows on CUDA when symmetric memory is available, else None (NCCL allreduce)."""
     if device.type != "cuda":
@@ -139,8 +203,10 @@ class ShardedSalsaState:
         self.FI_a = torch.zeros((self.dir_a.block_size, self.Dp), dtype=torch.float32, device=dev)
         self.ident = torch.arange(max(self.dir_a.block_size, self.dir_b.block_size),
                                   dtype=torch.int64, device=dev)
-        self.sym = make_symmetric_rows(max(self.dir_a.block_size, self.dir_b.block_size),
-                                       self.Dp, dev, group)
+        self.p2p = make_p2p_rows(max(self.dir_a.block_size, self.dir_b.block_size), self.Dp,
+                                 dev, group)
+        self.sym = None if self.p2p is not None else make_symmetric_rows(
+            max(self.dir_a.block_size, self.dir_b.block_size), self.Dp, dev, group)
         self.momentum = float(cfg.momentum)
         self.lrate = float(np.float32(cfg.learning_rate))
         self.unbias = torch.empty(self.nb, dtype=torch.float32, device=dev)
@@ -192,19 +258,25 @@ class ShardedSalsaState:
             rows = self.dir_b.block_rows(perm_r, k)
             b = rows.numel()
             if b > 0:
-                assemble_rows(self.Ap, self.ra[0], self.ra[1], rows, self.FI_b[:b], self.group,
-                              self.sym)
-                ops.salsa_block_update(self.FI_b, self.ident[:b], self.Bp, self.dB, self.d,
+                FI = self._assemble(self.Ap, self.ra, rows, self.FI_b[:b])
+                ops.salsa_block_update(FI, self.ident[:b], self.Bp, self.dB, self.d,
                                        self.dir_b.block_rowptr(k), self.dir_b.ent, self.momentum,
                                        self.lrate, self.unbias[k:k + 1], self.prec, self.ws_b)
             rows = self.dir_a.block_rows(perm_c, k)
             b = rows.numel()
             if b > 0:
-                assemble_rows(self.Bp, self.rb[0], self.rb[1], rows, self.FI_a[:b], self.group,
-                              self.sym)
-                ops.salsa_block_update(self.FI_a, self.ident[:b], self.Ap, self.dA, self.d,
+                FI = self._assemble(self.Bp, self.rb, rows, self.FI_a[:b])
+                ops.salsa_block_update(FI, self.ident[:b], self.Ap, self.dA, self.d,
                                        self.dir_a.block_rowptr(k), self.dir_a.ent, self.momentum,
                                        self.lrate, self.unbias[k:k + 1], self.prec, self.ws_a)
+        if self.p2p is not None:
+            self.p2p.pad_even(self.Ap)
+
+    def _assemble(self, local: Tensor, rng, rows: Tensor, out: Tensor) -> Tensor:
+        if self.p2p is not None:
+            return self.p2p.assemble(local, rng[0], rng[1], rows)
+        assemble_rows(local, rng[0], rng[1], rows, out, self.group, self.sym)
+        return out
 
     def factors(self) -> tuple[Tensor, Tensor]:
         """The whole factors (all-gathered), on every rank."""
