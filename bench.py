@@ -376,7 +376,7 @@ def run_ours(args):
                      "frac": achieved / tf32_peak,
                      # dram__bytes_read.sum + dram__bytes_write.sum of one launch at this shape
                      # (d = 16, TF32), ncu --set full: profiles/relu_product_c4_d16_tf32.md
-                     "traffic": 9.12e6 if (d == 16 and not x3 and args.config == "c4") else None,
+                     "traffic": 9.14e6 if (d == 16 and not x3 and args.config == "c4") else None,
                      "peak_source": f"{pk['source']} bf16 / 2 (dense TF32 rate)",
                      "tf32_matmul_measured_tflops": tf32_measured},
         "fused_reduce": reduce_line,
