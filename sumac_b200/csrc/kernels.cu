@@ -1072,6 +1072,140 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// Exclusive scan over the 1024 threads of a CTA; *total gets the sum.
+__device__ __forceinline__ int block_exclusive_scan_1024i(int v, int* wsum, int* total) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) wsum[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    const int ws = wsum[lane];
+    int x = ws;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int t = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += t;
+    }
+    wsum[lane] = x - ws;
+    if (lane == 31) wsum[32] = x;
+  }
+  __syncthreads();
+  const int r = wsum[w] + incl - v;
+  *total = wsum[32];
+  __syncthreads();  // wsum is reused by the next call
+  return r;
+}
+
+// Stable partition by block with the output staged in shared memory: per round of 8192 edges
+// (1024 threads x 8), warp w takes 256 consecutive edges (item-major) and ranks each within its
+// span and block (warp multisplit plus the warp's running count per block); one CTA-wide scan of
+// the [block][warp] counts orders the round by block, the round's (key, entry) pairs are written
+// to shared memory in that order, and then copied out so that consecutive threads write
+// consecutive positions of each block's run: coalesced stores, where the scatter kernels above
+// write 12-byte pieces into ~100 regions per round. Same output as csr_scatter_kernel.
+constexpr int CSR_STAGE_IT = 8;
+constexpr int CSR_STAGE_ROUND = 1024 * CSR_STAGE_IT;
+static size_t csr_stage_smem(int nb) {
+  return (size_t)CSR_STAGE_ROUND * (sizeof(int2) + sizeof(int32_t)) +
+         (size_t)(1 + 32 + 32 + 1) * nb * sizeof(int) + 64 * sizeof(int);
+}
+
+__global__ void __launch_bounds__(1024, 1)
+    csr_scatter_stage_kernel(const int32_t* __restrict__ e_fixed, const int32_t* __restrict__ e_out,
+                             const float* __restrict__ e_val, int64_t nnz, int64_t chunk,
+                             const int32_t* __restrict__ inv, int bs, int nb, int nbits, int64_t M,
+                             const int32_t* __restrict__ offs, int32_t* __restrict__ keys,
+                             int2* __restrict__ ent) {
+  extern __shared__ __align__(16) uint8_t smraw[];
+  int2* sent = reinterpret_cast<int2*>(smraw);                       // [ROUND]
+  int* skey = reinterpret_cast<int*>(sent + CSR_STAGE_ROUND);        // [ROUND]
+  int* base = skey + CSR_STAGE_ROUND;                                // [nb]
+  int* wcnt = base + nb;                                             // [32][nb]
+  int* pre = wcnt + 32 * nb;                                         // [nb][32]
+  int* off = pre + 32 * nb;                                          // [nb + 1]
+  int* wsum = off + nb + 1;                                          // [33]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int k = threadIdx.x; k < nb; k += blockDim.x) base[k] = offs[(int64_t)k * gridDim.x + blockIdx.x];
+  const int64_t e0 = (int64_t)blockIdx.x * chunk;
+  const int64_t e1 = min(nnz, e0 + chunk);
+  const unsigned lt_mask = (1u << lane) - 1u;
+  const int ns = nb * 32;
+  const int per = (ns + 1023) / 1024;
+  const int q0 = min(ns, (int)threadIdx.x * per), q1 = min(ns, q0 + per);
+  for (int64_t rb = e0; rb < e1; rb += CSR_STAGE_ROUND) {
+    for (int k = lane; k < nb; k += 32) wcnt[warp * nb + k] = 0;
+    __syncwarp();
+    int blk[CSR_STAGE_IT], loc[CSR_STAGE_IT], rnk[CSR_STAGE_IT];
+#pragma unroll
+    for (int j = 0; j < CSR_STAGE_IT; ++j) {
+      const int64_t e = rb + warp * (32 * CSR_STAGE_IT) + j * 32 + lane;
+      blk[j] = e < e1 ? e_fixed[e] : -1;
+    }
+#pragma unroll
+    for (int j = 0; j < CSR_STAGE_IT; ++j) {
+      if (blk[j] >= 0) {
+        const int pos = inv[blk[j]];
+        blk[j] = pos / bs;
+        loc[j] = pos - blk[j] * bs;
+      } else {
+        blk[j] = nb;
+        loc[j] = 0;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < CSR_STAGE_IT; ++j) {
+      const unsigned peers = warp_peers(blk[j], nbits);
+      const int rank = __popc(peers & lt_mask);
+      const int run = blk[j] < nb ? wcnt[warp * nb + blk[j]] : 0;
+      rnk[j] = run + rank;
+      __syncwarp();
+      if (blk[j] < nb && rank == 0) wcnt[warp * nb + blk[j]] = run + __popc(peers);
+      __syncwarp();
+    }
+    __syncthreads();
+    // exclusive scan of the counts in [block][warp] order
+    int tsum = 0;
+    for (int q = q0; q < q1; ++q) tsum += wcnt[(q & 31) * nb + (q >> 5)];
+    int total;
+    int run = block_exclusive_scan_1024i(tsum, wsum, &total);
+    for (int q = q0; q < q1; ++q) {
+      pre[q] = run;
+      run += wcnt[(q & 31) * nb + (q >> 5)];
+    }
+    __syncthreads();
+    for (int k = threadIdx.x; k < nb; k += blockDim.x) off[k] = pre[k * 32];
+    if (threadIdx.x == 0) off[nb] = total;
+#pragma unroll
+    for (int j = 0; j < CSR_STAGE_IT; ++j) {
+      if (blk[j] < nb) {
+        const int64_t e = rb + warp * (32 * CSR_STAGE_IT) + j * 32 + lane;
+        const int sp = pre[blk[j] * 32 + warp] + rnk[j];
+        skey[sp] = (int32_t)((int64_t)blk[j] * M + e_out[e]);
+        sent[sp] = make_int2(loc[j], __float_as_int(e_val[e]));
+      }
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < total; t += blockDim.x) {
+      int lo = 0, hi = nb;  // the block b with off[b] <= t < off[b + 1]
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (off[mid] <= t) lo = mid; else hi = mid;
+      }
+      const int gp = base[lo] + t - off[lo];
+      keys[gp] = skey[t];
+      ent[gp] = sent[t];
+    }
+    __syncthreads();
+    for (int k = threadIdx.x; k < nb; k += blockDim.x) base[k] += off[k + 1] - off[k];
+    __syncthreads();
+  }
+}
+
 __global__ void csr_scatter_kernel(const int32_t* __restrict__ e_fixed, const int32_t* __restrict__ e_out,
                                    const float* __restrict__ e_val, int64_t nnz, int64_t chunk,
                                    const int32_t* __restrict__ inv, int bs, int nb, int64_t M,
@@ -1220,6 +1354,22 @@ int launch_block_csr(const int64_t* perm, int64_t m_fixed, int num_blocks, const
     // (up to 1024 blocks: the new bases are formed four per thread)
     const size_t smem4 = (size_t)(1 + 32) * num_blocks * sizeof(int);
     const size_t smem1 = (size_t)(1 + 8) * num_blocks * sizeof(int);
+    const size_t smem_st = csr_stage_smem(num_blocks);
+    if (smem_st <= 200 * 1024) {
+      // largest opt-in so far per device (set on the first, eager, call of a shape)
+      static int stage_smem_set[64] = {};
+      int dev = 0;
+      cudaGetDevice(&dev);
+      if (dev < 0 || dev >= 64 || (int)smem_st > stage_smem_set[dev]) {
+        cudaFuncSetAttribute(csr_scatter_stage_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem_st);
+        if (dev >= 0 && dev < 64) stage_smem_set[dev] = (int)smem_st;
+      }
+      count_launch();
+      csr_scatter_stage_kernel<<<L.ncta, 1024, smem_st, stream>>>(
+          e_fixed, e_out, e_val, nnz, L.chunk, inv, bs, num_blocks, nbits, M, hist, keys, ent);
+      goto scattered;
+    }
     if (smem4 <= 48 * 1024) {
       count_launch();
       csr_scatter_tile_kernel<4><<<L.ncta, CSR_THREADS, smem4, stream>>>(
