@@ -786,7 +786,8 @@ void launch_finalize(const FinalizeArgs& a, cudaStream_t stream) {
   if (a.M == 0) return;
   const int threads = 256;
   const int G = a.Dp / 4 < 32 ? a.Dp / 4 : 32;
-  const unsigned grid = grid_cap(a.M * G, threads, 148 * 8);
+  // one wave: 4 resident CTAs per SM (64 registers); measured 22.5 us at C4 against 23.6 (2 waves)
+  const unsigned grid = grid_cap(a.M * G, threads, 148 * 4);
   count_launch();
   if (a.ginv) {
     switch (a.Dp) {
