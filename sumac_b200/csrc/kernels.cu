@@ -328,7 +328,6 @@ __global__ void __launch_bounds__(256) salsa_ginv_kernel(
     int* __restrict__ piv, float* __restrict__ ginv, int* err) {
   __shared__ float srow[PREP_ROWS * (D + 1)];
   __shared__ double aug[2][D][2 * D];  // [G | I] and its Gauss-Jordan iterates (double-buffered)
-  __shared__ int s_piv;
   __shared__ bool last;
   const int dd = d * d;
   // this CTA's rows [r0, r1), staged PREP_ROWS at a time; each thread keeps its entries' sums
@@ -389,15 +388,17 @@ __global__ void __launch_bounds__(256) salsa_ginv_kernel(
   __syncthreads();
   // G^{-1} by Gauss-Jordan elimination of [G | I] with partial pivoting (at step k the row, at or
   // below k, of largest |entry| in column k, the first on ties: getrf's pivot choice). Every
-  // thread updates its elements of the augmented matrix from the previous iterate; two barriers
+  // thread updates its elements of the augmented matrix from the previous iterate; one barrier
   // per step. Rows and columns beyond d stay the identity.
   (void)LU;
   (void)piv;
+  int piv_row = 0;
   for (int k = 0; k < d; ++k) {
     double(*cur)[2 * D] = aug[k & 1];
     double(*nxt)[2 * D] = aug[(k + 1) & 1];
-    if (threadIdx.x < 32) {
-      const int i = threadIdx.x;
+    {
+      // every warp finds the pivot row itself (no extra barrier)
+      const int i = threadIdx.x & 31;
       double v = (i >= k && i < d) ? fabs(cur[i][k]) : -1.0;
       int idx = i;
 #pragma unroll
@@ -406,13 +407,10 @@ __global__ void __launch_bounds__(256) salsa_ginv_kernel(
         const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
         if (ov > v || (ov == v && oi < idx)) { v = ov; idx = oi; }
       }
-      if (i == 0) {
-        s_piv = idx;
-        if (v == 0.0 && err) atomicCAS(err, 0, DEV_SINGULAR);
-      }
+      if (threadIdx.x == 0 && v == 0.0 && err) atomicCAS(err, 0, DEV_SINGULAR);
+      piv_row = idx;
     }
-    __syncthreads();
-    const int pr = s_piv;
+    const int pr = piv_row;
     const double inv = 1.0 / cur[pr][k];
     for (int e = threadIdx.x; e < D * 2 * D; e += blockDim.x) {
       const int i = e / (2 * D), j = e - i * (2 * D);
