@@ -24,7 +24,12 @@ from .salsa import draw_perm, init_salsa_factors
 class _Optimizer:
     """torch.optim semantics over the padded factors (training/gd.py:20-46)."""
 
-    def __init__(self, cfg: SumacConfig, params: list[Tensor], grads: list[Tensor], d: int):
+    def __init__(self, cfg: SumacConfig, params: list[Tensor], grads: list[Tensor], d: int,
+                 sum_group=None):
+        """sum_group: the last param / grad is this rank's slice of a factor sharded over the
+        group (the others are replicated): SGD's clipping norm adds the slices' squared norms
+        over the group."""
+        self.sum_group = sum_group
         self.cfg = cfg
         self.params = params
         self.grads = grads
@@ -57,8 +62,15 @@ class _Optimizer:
         elif self.kind == OptimizerName.SGD:
             # clip_grad_norm_([A, B], max_norm=1.0) then SGD with momentum (gd.py:43-46)
             self.sumsq.zero_()
-            for g in self.grads:
-                ops.grad_sumsq(g, self.sumsq)
+            if self.sum_group is not None:
+                import torch.distributed as dist
+                ops.grad_sumsq(self.grads[-1], self.sumsq)
+                dist.all_reduce(self.sumsq, group=self.sum_group)
+                for g in self.grads[:-1]:
+                    ops.grad_sumsq(g, self.sumsq)
+            else:
+                for g in self.grads:
+                    ops.grad_sumsq(g, self.sumsq)
             for p, g, buf in zip(self.params, self.grads, self.buf):
                 ops.sgd_step(p, g, buf, cfg.learning_rate, cfg.momentum, t == 1, self.sumsq, 1.0)
         else:

@@ -28,7 +28,7 @@ import torch.distributed as dist
 from torch import Tensor
 
 from . import _native, ops
-from .config import SumacConfig
+from .config import OptimizerName, SumacConfig
 from .data import SparseDirection
 from .metrics import Evaluator
 from .salsa import GRAPH_MIN_ITERATIONS, draw_perm, init_salsa_factors, unbias_values
@@ -358,13 +358,15 @@ def virtual_positions(pos: Tensor, m: int, nb: int, rank: int, world: int) -> Te
 
 
 def combine_block_grads(gA: Tensor, gB: Tensor, block_rows: list[Tensor], gbuf: Tensor,
-                        group=None) -> None:
+                        group=None, reduce_b: bool = True) -> None:
     """Complete the gradients of one GD step whose row blocks were split over the ranks: each
     rank holds grad A on the rows of its sub-blocks (zero on the other rows of the blocks) and a
     partial grad B over its sub-blocks' entries. grad B is the sum of the partials (allreduce);
     the blocks' rows of grad A are disjoint between ranks, so their sum (an allreduce of the
-    gathered rows) is exact. Afterwards every rank holds the whole step's gradients."""
-    dist.all_reduce(gB, group=group)
+    gathered rows) is exact. Afterwards every rank holds the whole step's gradients (grad B
+    only with reduce_b; otherwise the caller reduce-scatters it)."""
+    if reduce_b:
+        dist.all_reduce(gB, group=group)
     for full in block_rows:
         b = full.numel()
         if b == 0:
@@ -394,10 +396,24 @@ class ShardedGDState:
         self.Dp = Dp = ops.padded_rank(d)
         self.prec = cfg.precision()
         self.Ap = ops.pad_factor(A.detach().to(torch.float32), Dp)
-        self.Bp = ops.pad_factor(B.detach().to(torch.float32), Dp)
         self.gA = torch.zeros_like(self.Ap)
-        self.gB = torch.zeros_like(self.Bp)
-        self.opt = _Optimizer(cfg, [self.Ap, self.Bp], [self.gA, self.gB], d)
+        # B, grad B: n rows padded to a multiple of the world size, so that grad B can be
+        # reduce-scattered into equal row slices and B all-gathered back from them
+        chunk = (n + self.world - 1) // self.world
+        self.Bfull = torch.zeros((chunk * self.world, Dp), dtype=torch.float32, device=dev)
+        self.Bfull[:n, :d] = B.detach().to(torch.float32)
+        self.gBfull = torch.zeros_like(self.Bfull)
+        self.Bp, self.gB = self.Bfull[:n], self.gBfull[:n]
+        # ZeRO-1 for B (Adam, AdamW, SGD: elementwise steps): each rank steps only its slice of B
+        # and keeps only that slice's optimizer state; Muon (whole-matrix step) stays replicated
+        self.zero_b = cfg.optimizer in (OptimizerName.ADAM, OptimizerName.ADAMW, OptimizerName.SGD)
+        if self.zero_b:
+            self.Bslice = self.Bfull[self.rank * chunk:(self.rank + 1) * chunk]
+            self.gBslice = torch.zeros_like(self.Bslice)
+            self.opt = _Optimizer(cfg, [self.Ap, self.Bslice], [self.gA, self.gBslice], d,
+                                  sum_group=group)
+        else:
+            self.opt = _Optimizer(cfg, [self.Ap, self.Bp], [self.gA, self.gB], d)
         self.m, self.n = m, n
         nb = self.nb = cfg.num_blocks
         perm = draw_perm(m, gen_blocks, dev)     # the same partition on every rank
@@ -456,8 +472,14 @@ class ShardedGDState:
             if first:
                 ops.fill_zero(gB)
             combine_block_grads(gA, gB, [self.blocks[k][1] for k in batch], self.gbuf,
-                                self.group)
-            self.opt.step()
+                                self.group, reduce_b=not self.zero_b)
+            if self.zero_b:
+                # reduce-scatter grad B (sum) -> step this rank's slice -> all-gather B
+                dist.reduce_scatter_tensor(self.gBslice, self.gBfull, group=self.group)
+                self.opt.step()
+                dist.all_gather_into_tensor(self.Bfull, self.Bslice, group=self.group)
+            else:
+                self.opt.step()
         if report:
             dist.all_reduce(self.terms, group=self.group)
 
