@@ -321,6 +321,77 @@ __global__ void __launch_bounds__(256) salsa_gather_kernel(
   }
 }
 
+// G^{-1} by Gauss-Jordan elimination of [G | I] (a0: D x 2D, fp64) held in one warp's registers:
+// lane l keeps column l of the 32 columns, all D rows. At step k column k is broadcast from its
+// lane, every lane picks the pivot row (largest |entry| at or below k, the first on ties:
+// getrf's choice, with magnitudes compared in fp32) and updates its column: row k <- pivot row /
+// pivot, row pr <- old row k, other rows r <- r - r[k] * (new row k). No CTA barrier inside the
+// elimination; the step's dependent chain is short because fp64 operations have long latency.
+__device__ __forceinline__ void warp_gauss_jordan16(const double (*a0)[32], int d, int Dp,
+                                                    float* ginv, int* err) {
+  constexpr int D = 16;
+  const int lane = threadIdx.x & 31;
+  double c[D];
+#pragma unroll
+  for (int i = 0; i < D; ++i) c[i] = a0[i][lane];
+  for (int k = 0; k < d; ++k) {
+    double colk[D];
+    float mag[D];
+    int id[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) {
+      colk[i] = __shfl_sync(0xffffffffu, c[i], k);
+      mag[i] = (i >= k && i < d) ? fabsf((float)colk[i]) : -1.f;
+      id[i] = i;
+    }
+    // pivot: largest magnitude (compared in fp32), the first on ties, by a tree over the rows
+    // (the lower-index half always on the left) instead of a chain of dependent fp64 compares
+#pragma unroll
+    for (int w = 1; w < D; w <<= 1) {
+#pragma unroll
+      for (int i = 0; i + w < D; i += 2 * w) {
+        if (mag[i + w] > mag[i]) { mag[i] = mag[i + w]; id[i] = id[i + w]; }
+      }
+    }
+    const int idx = id[0];
+    if (lane == 0 && mag[0] == 0.f && err) atomicCAS(err, 0, DEV_SINGULAR);
+    double pv = 0.0, ck = 0.0, cpr = 0.0, ckk = 0.0;
+#pragma unroll
+    for (int i = 0; i < D; ++i) {
+      if (i == idx) { pv = colk[i]; cpr = c[i]; }
+      if (i == k) { ckk = colk[i]; ck = c[i]; }
+    }
+    // 1 / pv: fp32 seed refined by two Newton-Raphson steps r <- r + r (1 - pv r) (each doubles
+    // the correct bits: 2^-23 -> 2^-46 -> fp64 rounding); IEEE division where the seed is not
+    // finite (|pv| outside the fp32 range)
+    double inv = (double)(1.0f / (float)pv);
+    if (isfinite(inv) && inv != 0.0) {
+      inv = fma(inv, fma(-pv, inv, 1.0), inv);
+      inv = fma(inv, fma(-pv, inv, 1.0), inv);
+    } else {
+      inv = 1.0 / pv;
+    }
+    const double rowk = cpr * inv;  // this lane's entry of the pivot row, moved to k and scaled
+#pragma unroll
+    for (int i = 0; i < D; ++i) {
+      const double sv = (i == idx) ? ck : c[i];      // row pr takes the old row k
+      const double sk = (i == idx) ? ckk : colk[i];
+      c[i] = (i == k) ? rowk : sv - sk * rowk;
+    }
+  }
+  // columns D..2D-1 hold G^{-1}: lane D + col writes column col
+  if (lane >= D) {
+    const int col = lane - D;
+    for (int k = 0; k < Dp; ++k) {
+      double v = 0.0;
+#pragma unroll
+      for (int i = 0; i < D; ++i)
+        if (i == k) v = c[i];
+      ginv[k * Dp + col] = (k < d && col < d) ? (float)v : 0.f;
+    }
+  }
+}
+
 template <int D>
 __global__ void __launch_bounds__(256) salsa_ginv_kernel(
     const float* __restrict__ FI, int64_t b, int d, int Dp, int64_t rows_per_cta,
@@ -350,14 +421,17 @@ __global__ void __launch_bounds__(256) salsa_ginv_kernel(
       const int e = threadIdx.x + q * 256;
       if (e < dd) {
         const int i = e / d, j = e - i * d;
-        double s0 = 0.0, s1 = 0.0;
+        // four independent fp64 chains (fp64 latency, not throughput, bounds this loop)
+        double s0 = 0.0, s1 = 0.0, s2 = 0.0, s3 = 0.0;
         int rr = 0;
-        for (; rr + 1 < nr; rr += 2) {
+        for (; rr + 3 < nr; rr += 4) {
           s0 += (double)srow[rr * (D + 1) + i] * (double)srow[rr * (D + 1) + j];
           s1 += (double)srow[(rr + 1) * (D + 1) + i] * (double)srow[(rr + 1) * (D + 1) + j];
+          s2 += (double)srow[(rr + 2) * (D + 1) + i] * (double)srow[(rr + 2) * (D + 1) + j];
+          s3 += (double)srow[(rr + 3) * (D + 1) + i] * (double)srow[(rr + 3) * (D + 1) + j];
         }
-        if (rr < nr) s0 += (double)srow[rr * (D + 1) + i] * (double)srow[rr * (D + 1) + j];
-        acc[q] += s0 + s1;
+        for (; rr < nr; ++rr) s0 += (double)srow[rr * (D + 1) + i] * (double)srow[rr * (D + 1) + j];
+        acc[q] += (s0 + s1) + (s2 + s3);
       }
     }
   }
@@ -386,6 +460,11 @@ __global__ void __launch_bounds__(256) salsa_ginv_kernel(
     aug[0][i][j] = v;
   }
   __syncthreads();
+  if constexpr (D == 16) {
+    if (threadIdx.x < 32) warp_gauss_jordan16(aug[0], d, Dp, ginv, err);
+    if (threadIdx.x == 0) *counter = 0u;  // ready for the next launch (graph replays included)
+    return;
+  }
   // G^{-1} by Gauss-Jordan elimination of [G | I] with partial pivoting (at step k the row, at or
   // below k, of largest |entry| in column k, the first on ties: getrf's pivot choice). Every
   // thread updates its elements of the augmented matrix from the previous iterate; one barrier
@@ -548,8 +627,8 @@ __device__ __forceinline__ float support_coef(int mode, float val, float L) {
 }
 
 template <int DP, bool GINV>
-// 64 registers (4 CTAs of 256 threads per SM): the pass is latency-bound, warps in flight matter
-__global__ void __launch_bounds__(256, 4) finalize_kernel(FinalizeArgs a) {
+// 80 registers (3 CTAs of 256 threads per SM): room for the heavy rows' entries in flight
+__global__ void __launch_bounds__(256, 3) finalize_kernel(FinalizeArgs a) {
   constexpr int G = DP / 4 < 32 ? DP / 4 : 32;  // lanes per row
   constexpr int V = DP / 4 / G;                  // float4 slices per lane
   constexpr int RPW = 32 / G;                    // rows per warp
@@ -647,17 +726,20 @@ __global__ void __launch_bounds__(256, 4) finalize_kernel(FinalizeArgs a) {
                                 __shfl_sync(0xffffffffu, x[v].z, sl), __shfl_sync(0xffffffffu, x[v].w, sl));
             hcor[v] = make_float4(0.f, 0.f, 0.f, 0.f);
           }
-          for (int q0 = 0; q0 < hn; q0 += 2 * RPW) {
-            int2 en[2];
-            float4 f[2][V], c[2][V];
-            float part[2];
+          // HU entries per lane group and round (entry q0 + u * RPW + gw), the next round's
+          // entries loaded before this round's F / C gathers
+          constexpr int HU = 4;
+          int2 en[HU];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int q = q0 + u * RPW + gw;
-              en[u] = q < hn ? a.ent[hb + q] : make_int2(0, 0);
-            }
+          for (int u = 0; u < HU; ++u) {
+            const int q = u * RPW + gw;
+            en[u] = q < hn ? a.ent[hb + q] : make_int2(0, 0);
+          }
+          for (int q0 = 0; q0 < hn; q0 += HU * RPW) {
+            float4 f[HU][V], c[HU][V];
+            float part[HU];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) {
+            for (int u = 0; u < HU; ++u) {
               const bool has = q0 + u * RPW + gw < hn;
               const float4* frow = reinterpret_cast<const float4*>(a.F + (int64_t)en[u].x * DP);
               const float4* crow = reinterpret_cast<const float4*>(a.Cm + (int64_t)en[u].x * DP);
@@ -667,17 +749,25 @@ __global__ void __launch_bounds__(256, 4) finalize_kernel(FinalizeArgs a) {
                 c[u][v] = has ? crow[gl + v * G] : make_float4(0.f, 0.f, 0.f, 0.f);
               }
             }
+            int2 enx[HU];
 #pragma unroll
-            for (int u = 0; u < 2; ++u) part[u] = dot4v<V>(hx, f[u]);
+            for (int u = 0; u < HU; ++u) {
+              const int q = q0 + HU * RPW + u * RPW + gw;
+              enx[u] = q < hn ? a.ent[hb + q] : make_int2(0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < HU; ++u) part[u] = dot4v<V>(hx, f[u]);
 #pragma unroll
             for (int o = G / 2; o > 0; o >>= 1) {
 #pragma unroll
-              for (int u = 0; u < 2; ++u) part[u] += __shfl_xor_sync(0xffffffffu, part[u], o);
+              for (int u = 0; u < HU; ++u) part[u] += __shfl_xor_sync(0xffffffffu, part[u], o);
             }
 #pragma unroll
-            for (int u = 0; u < 2; ++u)
+            for (int u = 0; u < HU; ++u) {
               if (q0 + u * RPW + gw < hn)
                 axpy4v<V>(support_coef(a.mode, __int_as_float(en[u].y), part[u]), c[u], hcor);
+              en[u] = enx[u];
+            }
           }
 #pragma unroll
           for (int o = G; o < 32; o <<= 1) {
@@ -784,8 +874,8 @@ void launch_finalize(const FinalizeArgs& a, cudaStream_t stream) {
   if (a.M == 0) return;
   const int threads = 256;
   const int G = a.Dp / 4 < 32 ? a.Dp / 4 : 32;
-  // one wave: 4 resident CTAs per SM (64 registers); measured 22.5 us at C4 against 23.6 (2 waves)
-  const unsigned grid = grid_cap(a.M * G, threads, 148 * 4);
+  // one wave: 3 resident CTAs per SM (80 registers)
+  const unsigned grid = grid_cap(a.M * G, threads, 148 * 3);
   count_launch();
   if (a.ginv) {
     switch (a.Dp) {
