@@ -272,6 +272,7 @@ __global__ void __launch_bounds__(256) salsa_gather_kernel(
     float* __restrict__ FI, float* __restrict__ Fhi, float* __restrict__ Flo,
     float* __restrict__ Cthi, float* __restrict__ Ctlo, int64_t ldct, unsigned int* stats) {
   extern __shared__ float tile[];  // [32][Dp + 1]
+  pdl_trigger();  // the product may launch now; it waits for this grid before reading its output
   const int64_t r0 = (int64_t)blockIdx.x * 32;
   const int nr = (int)min((int64_t)32, b - r0);
   const int ld = Dp + 1;
@@ -629,6 +630,7 @@ __device__ __forceinline__ float support_coef(int mode, float val, float L) {
 template <int DP, bool GINV>
 // 80 registers (3 CTAs of 256 threads per SM): room for the heavy rows' entries in flight
 __global__ void __launch_bounds__(256, 3) finalize_kernel(FinalizeArgs a) {
+  pdl_wait();  // launched programmatically behind the product: its partials must be complete
   constexpr int G = DP / 4 < 32 ? DP / 4 : 32;  // lanes per row
   constexpr int V = DP / 4 / G;                  // float4 slices per lane
   constexpr int RPW = 32 / G;                    // rows per warp
@@ -879,18 +881,18 @@ void launch_finalize(const FinalizeArgs& a, cudaStream_t stream) {
   count_launch();
   if (a.ginv) {
     switch (a.Dp) {
-      case 16: finalize_kernel<16, true><<<grid, threads, 0, stream>>>(a); break;
-      case 32: finalize_kernel<32, true><<<grid, threads, 0, stream>>>(a); break;
+      case 16: launch_pdl(finalize_kernel<16, true>, grid, threads, 0, stream, a); break;
+      case 32: launch_pdl(finalize_kernel<32, true>, grid, threads, 0, stream, a); break;
       default: break;
     }
     return;
   }
   switch (a.Dp) {
-    case 16: finalize_kernel<16, false><<<grid, threads, 0, stream>>>(a); break;
-    case 32: finalize_kernel<32, false><<<grid, threads, 0, stream>>>(a); break;
-    case 64: finalize_kernel<64, false><<<grid, threads, 0, stream>>>(a); break;
-    case 128: finalize_kernel<128, false><<<grid, threads, 0, stream>>>(a); break;
-    case 256: finalize_kernel<256, false><<<grid, threads, 0, stream>>>(a); break;
+    case 16: launch_pdl(finalize_kernel<16, false>, grid, threads, 0, stream, a); break;
+    case 32: launch_pdl(finalize_kernel<32, false>, grid, threads, 0, stream, a); break;
+    case 64: launch_pdl(finalize_kernel<64, false>, grid, threads, 0, stream, a); break;
+    case 128: launch_pdl(finalize_kernel<128, false>, grid, threads, 0, stream, a); break;
+    case 256: launch_pdl(finalize_kernel<256, false>, grid, threads, 0, stream, a); break;
     default: break;
   }
 }

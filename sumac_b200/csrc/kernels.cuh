@@ -9,6 +9,28 @@ namespace sb {
 
 // Number of kernels this library has launched (all threads, all devices).
 void count_launch();
+
+// Programmatic dependent launch: a kernel launched with launch_pdl may start while the previous
+// kernel of its stream drains; it calls pdl_wait() before it reads anything that kernel wrote
+// (a no-op when the launch had no programmatic dependency). pdl_trigger() lets the next
+// programmatic launch of the stream start before this kernel ends.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
 long long launch_count();
 
 // ---- fused product / reduce (product.cu) ---------------------------------------------------

@@ -149,8 +149,9 @@ static int run_kernel(const CUtensorMap& mx, const CUtensorMap& mfh, const CUten
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   count_launch();
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, stream>>>(mx, mfh, mfl, mch, mcl, p);
-  return (int)cudaGetLastError();
+  const cudaError_t e = launch_pdl(kern, dim3(grid), dim3(Cfg::THREADS), Cfg::SMEM_BYTES, stream,
+                                   mx, mfh, mfl, mch, mcl, p);
+  return e != cudaSuccess ? (int)e : (int)cudaGetLastError();
 }
 
 #define SB_PRODUCT_CASE(DPV, BNV, STV, X3V, REDV, GV)                                          \

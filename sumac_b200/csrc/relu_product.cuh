@@ -356,6 +356,9 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
       if (X3) tma_prefetch_desc(&tmClo);
     }
   }
+  // launched programmatically behind the operand gather: its output is read from here on, and
+  // the TMEM allocation waits too (so it never overlaps a previous product of the stream)
+  pdl_wait();
   if (warp == 1) tmem_alloc(tmem_slot, 512);
   tc_fence_before();
   __syncthreads();

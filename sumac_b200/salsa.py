@@ -114,7 +114,13 @@ def unbias_values(momentum: float, first_step: int, count: int) -> np.ndarray:
                      for s in range(first_step, first_step + count)], dtype=np.float32)
 
 
-GRAPH_MIN_ITERATIONS = 40
+# A CUDA graph of the iteration pays off over many iterations only: at C4 the first capture and
+# instantiation in a process costs ~0.25 s and a replay saves ~8 % of an eager iteration (62.5
+# against 57.7 iterations/s), so eager launches win below ~190 iterations.
+GRAPH_MIN_ITERATIONS = 200
+# Sharded runs: a rank's eager launches of the exchange and block updates cost more host time
+# than its shorter device work, so their graph pays off sooner.
+GRAPH_MIN_ITERATIONS_SHARDED = 40
 
 
 class SalsaState:
@@ -217,8 +223,6 @@ def salsa_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: SumacConfi
     else:
         A, B = A_init.to(dev), B_init.to(dev)
     st = SalsaState(S_index, S_value, m, n, cfg, A, B, dirs=dirs)
-    # a CUDA graph of the iteration pays off over many iterations only (capturing ~800 launches
-    # costs about two iterations; a replay saves ~5 % of one)
     st.use_graph = cfg.max_iterations >= GRAPH_MIN_ITERATIONS
     evaluator = Evaluator(S_index, S_value, cfg.rank, st.prec)
     # the reference's datasets draw one permutation each at construction (datasets.py:34)

@@ -31,7 +31,7 @@ from . import _native, ops
 from .config import OptimizerName, SumacConfig
 from .data import SparseDirection
 from .metrics import Evaluator
-from .salsa import GRAPH_MIN_ITERATIONS, draw_perm, init_salsa_factors, unbias_values
+from .salsa import GRAPH_MIN_ITERATIONS_SHARDED, draw_perm, init_salsa_factors, unbias_values
 
 
 def shard_range(total: int, rank: int, world: int) -> tuple[int, int]:
@@ -299,7 +299,7 @@ def sharded_salsa_loop(S_index: Tensor, S_value: Tensor, m: int, n: int, cfg: Su
     else:
         A, B = A_init.to(dev), B_init.to(dev)
     st = ShardedSalsaState(S_index, S_value, m, n, cfg, A, B, group)
-    st.use_graph = cfg.max_iterations >= GRAPH_MIN_ITERATIONS
+    st.use_graph = cfg.max_iterations >= GRAPH_MIN_ITERATIONS_SHARDED
     evaluator = Evaluator(S_index, S_value, cfg.rank, st.prec)
     draw_perm(m, gen_rows, dev)
     draw_perm(n, gen_cols, dev)
