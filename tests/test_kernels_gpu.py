@@ -127,6 +127,43 @@ def test_salsa_block_update(d, m_fixed, b, M, nnz, prec):
 
 
 @pytest.mark.parametrize("prec", PRECS)
+@pytest.mark.parametrize("d", [16, 32, 64])
+def test_salsa_block_update_heavy_rows(d, prec):
+    """Power-law rows: the finalize pass hands a row's entries beyond the first eight to the whole
+    warp, several rounds of entries per row, with the next round's entries loaded ahead. Rows with
+    up to ~300 entries, several heavy rows in one warp's batch and a heavy last row."""
+    rng = np.random.default_rng(100 + d)
+    m_fixed, b, M = 3000, 400, 1000
+    Dp = ops.padded_rank(d)
+    F = rng.standard_normal((m_fixed, d)).astype(np.float32)
+    X = (0.3 * rng.standard_normal((M, d))).astype(np.float32)
+    dX = (0.05 * rng.standard_normal((M, d))).astype(np.float32)
+    rows = rng.choice(m_fixed, size=b, replace=False)
+    heavy = {0: 300, 1: 170, 2: 41, 3: 9, 5: 64, 7: 33, 8: 97, 123: 250, M - 1: 129}
+    li_l, oj_l = [], []
+    for r, k in heavy.items():
+        li_l.append(rng.choice(b, size=k, replace=False))
+        oj_l.append(np.full(k, r))
+    li_r, oj_r, _ = random_edges(rng, b, M, 6000)
+    keep = ~np.isin(oj_r, list(heavy))
+    li = np.concatenate(li_l + [li_r[keep]]).astype(np.int64)
+    oj = np.concatenate(oj_l + [oj_r[keep]]).astype(np.int64)
+    v = (0.05 + rng.random(li.size)).astype(np.float32)
+    rowptr, ent = host_csr(li, oj, v, M)
+    mu, lr, step = 0.7, 0.1, 3
+    unbias = np.float32(1.0) - np.float32(mu) ** np.float32(step)
+    Xd, dXd = to_dev(pad(X, Dp)), to_dev(pad(dX, Dp))
+    ops.salsa_block_update(to_dev(pad(F, Dp)), to_dev(rows), Xd, dXd, d, to_dev(rowptr),
+                           to_dev(ent), mu, lr, to_dev(np.array([unbias], np.float32)), prec)
+    _native.raise_device_error(0)
+    A_I = F[rows].astype(np.float64)
+    Bn, dBn = orc.lsq_update(A_I, X, orc.pinv_t(A_I), dX, li, oj, v, mu, float(unbias), lr)
+    tol = 1e-4 if prec == ops.SUMAC_3XTF32 else 1e-3
+    assert rel_err(dXd.cpu().numpy()[:, :d], dBn) < tol
+    assert_close_elementwise(Xd.cpu().numpy()[:, :d], Bn, tol, tol)
+
+
+@pytest.mark.parametrize("prec", PRECS)
 @pytest.mark.parametrize("d,m,n,b,nnz", [(8, 2000, 1500, 2000, 40000), (16, 900, 3000, 300, 20000),
                                          (32, 500, 700, 129, 3000), (128, 400, 500, 200, 4000),
                                          (256, 300, 400, 150, 3000)])
