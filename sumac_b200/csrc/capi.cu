@@ -348,7 +348,9 @@ static SalsaPlan plan_salsa(void* ws, int64_t M, int64_t b, int d, int Dp, bool 
   const size_t pbytes = d <= 32 ? salsa_ginv_scratch_bytes(b, d) : 0;
   p.gram = bp.take<double>(((gbytes > pbytes ? gbytes : pbytes) + 7) / 8);
   p.ginv = bp.take<float>((size_t)Dp * Dp);
-  p.counter = bp.take<unsigned int>(64);  // [0] done-CTA counter, [1..2] operand maxima
+  // [0] Gram-inverse done-CTA counter; from [2]: one (max |F_i|, max |C|) pair per gather CTA
+  // (the d > 32 path: one atomically maxed pair at [1..2])
+  p.counter = bp.take<unsigned int>(4 + 2 * (size_t)salsa_gather_ctas(b));
   // the split count grows as b shrinks; size for the worst case over b' <= b
   int smax = 1;
   for (int64_t bb = b; bb > 0; bb = bb / 2) {
@@ -392,9 +394,9 @@ int sumac_salsa_block_update(const float* F, int64_t m_fixed, const int64_t* row
     // the finalize pass applies G^{-1}, which a side stream computes while the product runs
     SideStream* side = side_stream();
     if (!side) return fail(SUMAC_ERR_CUDA, "salsa_block_update: side stream creation failed");
-    cudaMemsetAsync(p.counter, 0, 3 * sizeof(unsigned int), s);
+    // no memset: the gather writes every CTA's pair of operand maxima and zeroes the counter
     launch_salsa_gather(F, rows, b, Dp, p.FI, p.Fhi, p.Flo, p.Cthi, p.Ctlo, p.ldct,
-                        x3 ? nullptr : p.counter + 1, s);
+                        x3 ? nullptr : p.counter + 2, p.counter, s);
     cudaEventRecord(side->fork, s);
     cudaStreamWaitEvent(side->stream, side->fork, 0);
     launch_salsa_ginv(p.FI, b, d, Dp, p.gram, p.counter, p.ginv, dev_err, side->stream);
@@ -403,7 +405,8 @@ int sumac_salsa_block_update(const float* F, int64_t m_fixed, const int64_t* row
     // instead of sharing issue slots with product CTAs
     const int psms = sms > 2 * kGinvSms ? sms - kGinvSms : sms;
     int rc = launch_relu_product(X, M, p.Fhi, p.Flo, p.Cthi, p.Ctlo, p.ldct, b, Dp,
-                                 x3, p.part, dev_err, psms, g_timeout_ns, s, p.counter + 1, 0, 1);
+                                 x3, p.part, dev_err, psms, g_timeout_ns, s, p.counter + 2, 0, 1,
+                                 salsa_gather_ctas(b));
     cudaStreamWaitEvent(s, side->join, 0);
     if (rc) return cuda_status(rc, "salsa_block_update");
     FinalizeArgs f{};

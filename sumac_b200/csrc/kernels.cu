@@ -270,9 +270,14 @@ int salsa_gram_parts(int64_t b) { return cdiv64(b, PREP_ROWS) < 1 ? 1 : cdiv64(b
 __global__ void __launch_bounds__(256) salsa_gather_kernel(
     const float* __restrict__ Ffix, const int64_t* __restrict__ rows, int64_t b, int Dp,
     float* __restrict__ FI, float* __restrict__ Fhi, float* __restrict__ Flo,
-    float* __restrict__ Cthi, float* __restrict__ Ctlo, int64_t ldct, unsigned int* stats) {
+    float* __restrict__ Cthi, float* __restrict__ Ctlo, int64_t ldct, unsigned int* stats,
+    unsigned int* ginv_counter) {
   extern __shared__ float tile[];  // [32][Dp + 1]
+  __shared__ float wmax[2][8];
+  pdl_wait();     // launched programmatically behind the previous block update
   pdl_trigger();  // the product may launch now; it waits for this grid before reading its output
+  // the Gram-inverse launch of this update runs after this grid; the previous one has finished
+  if (blockIdx.x == 0 && threadIdx.x == 0 && ginv_counter) *ginv_counter = 0u;
   const int64_t r0 = (int64_t)blockIdx.x * 32;
   const int nr = (int)min((int64_t)32, b - r0);
   const int ld = Dp + 1;
@@ -315,12 +320,21 @@ __global__ void __launch_bounds__(256) salsa_gather_kernel(
       fm = fmaxf(fm, __shfl_xor_sync(0xffffffffu, fm, o));
       amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     }
+    // this CTA's pair: maxima over its warps (no atomics, so no zeroing before the launch)
     if ((threadIdx.x & 31) == 0) {
-      atomicMax(&stats[0], __float_as_uint(fm));
-      atomicMax(&stats[1], __float_as_uint(amax));
+      wmax[0][threadIdx.x >> 5] = fm;
+      wmax[1][threadIdx.x >> 5] = amax;
+    }
+    __syncthreads();
+    if (threadIdx.x < 2) {
+      float m = 0.f;
+      for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, wmax[threadIdx.x][w]);
+      stats[2 * blockIdx.x + threadIdx.x] = __float_as_uint(m);
     }
   }
 }
+
+int salsa_gather_ctas(int64_t b) { return (int)cdiv64(b > 0 ? b : 1, 32); }
 
 // G^{-1} by Gauss-Jordan elimination of [G | I] (a0: D x 2D, fp64) held in one warp's registers:
 // lane l keeps column l of the 32 columns, all D rows. At step k column k is broadcast from its
@@ -521,11 +535,12 @@ size_t salsa_ginv_scratch_bytes(int64_t b, int d) {
 
 void launch_salsa_gather(const float* Ffix, const int64_t* rows, int64_t b, int Dp, float* FI,
                          float* Fhi, float* Flo, float* Cthi, float* Ctlo, int64_t ldct,
-                         unsigned int* stats, cudaStream_t stream) {
+                         unsigned int* stats, unsigned int* ginv_counter,
+                         cudaStream_t stream) {
   const size_t smem = (size_t)32 * (Dp + 1) * sizeof(float);
   count_launch();
-  salsa_gather_kernel<<<cdiv64(b, 32), 256, smem, stream>>>(Ffix, rows, b, Dp, FI, Fhi, Flo, Cthi,
-                                                            Ctlo, ldct, stats);
+  launch_pdl(salsa_gather_kernel, dim3((unsigned)cdiv64(b, 32)), dim3(256), smem, stream, Ffix,
+             rows, b, Dp, FI, Fhi, Flo, Cthi, Ctlo, ldct, stats, ginv_counter);
 }
 
 void launch_salsa_ginv(const float* FI, int64_t b, int d, int Dp, void* scratch,

@@ -43,7 +43,7 @@ int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float
                         const float* Cthi, const float* Ctlo, int64_t ldct, int64_t N, int Dp,
                         bool x3, float* ws, int* err, int num_sms, unsigned long long timeout_ns,
                         cudaStream_t stream, const unsigned int* stats, int step = 0,
-                        int f_rounded = 0);
+                        int f_rounded = 0, int nstats = 1);
 // stats[0] = bits of max_r |F[r]| (row norm over Dp), stats[1] = bits of max |C| over nC values
 // (atomicMax on non-negative float bits; the words must be zero beforehand). The TF32 product
 // (fp16 second MMA) reads them to pick exact power-of-two scales.
@@ -80,15 +80,17 @@ void launch_solve(const float* FI, int64_t b, int d, int Dp, const double* gram_
 int salsa_gram_parts(int64_t b);
 
 // SALSA block step with C = F_I (d <= 32): gather F_I = Ffix[rows] (and its tf32 halves, its
-// transpose C^T = F_I^T split in 3xTF32 mode, and the operand maxima into stats[0..1], zero
-// before) in one launch; then G^{-1} of G = F_I^T F_I into ginv [Dp][Dp] (fp32) in one launch whose
-// last CTA factors G. scratch: salsa_ginv_scratch_bytes(b, d); counter zero before the first use.
+// transpose C^T = F_I^T split in 3xTF32 mode, and each CTA's operand maxima into its own pair
+// stats[2 * cta .. 2 * cta + 1], salsa_gather_ctas(b) pairs, no zeroing needed) in one launch,
+// which also zeroes the Gram-inverse counter; then G^{-1} of G = F_I^T F_I into ginv [Dp][Dp]
+// (fp32) in one launch whose last CTA factors G. scratch: salsa_ginv_scratch_bytes(b, d).
+int salsa_gather_ctas(int64_t b);
 // SMs the Gram-inverse launch uses beside the fused product, which then runs on num_sms - kGinvSms
 constexpr int kGinvSms = 11;
 size_t salsa_ginv_scratch_bytes(int64_t b, int d);
 void launch_salsa_gather(const float* Ffix, const int64_t* rows, int64_t b, int Dp, float* FI,
                          float* Fhi, float* Flo, float* Cthi, float* Ctlo, int64_t ldct,
-                         unsigned int* stats, cudaStream_t stream);
+                         unsigned int* stats, unsigned int* ginv_counter, cudaStream_t stream);
 void launch_salsa_ginv(const float* FI, int64_t b, int d, int Dp, void* scratch,
                        unsigned int* counter, float* ginv, int* err, cudaStream_t stream);
 

@@ -355,7 +355,8 @@ static int launch_simt(const float* X, int64_t M, const float* Fhi, const float*
 int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float* Flo,
                         const float* Cthi, const float* Ctlo, int64_t ldct, int64_t N, int Dp,
                         bool x3, float* ws, int* err, int num_sms, unsigned long long timeout_ns,
-                        cudaStream_t stream, const unsigned int* stats, int step, int f_rounded) {
+                        cudaStream_t stream, const unsigned int* stats, int step, int f_rounded,
+                        int nstats) {
   ProdCfgRt c = product_cfg(Dp, x3);
   if (!c.ok) return -1;
   if (M <= 0 || N <= 0 || M >= INT32_MAX || N >= INT32_MAX) return -5;
@@ -380,6 +381,7 @@ int launch_relu_product(const float* X, int64_t M, const float* Fhi, const float
   p.timeout_ns = timeout_ns;
   p.Xg = X;
   p.stats = stats;
+  p.nstats = nstats;
   p.step = step;
   p.count = 0;
   p.f_rounded = f_rounded;
@@ -410,6 +412,7 @@ int launch_relu_reduce(const float* X, int64_t M, const float* Fhi, const float*
   p.ws = nullptr;
   p.Xg = X;
   p.stats = nullptr;
+  p.nstats = 0;
   p.step = 0;
   p.count = count;
   p.f_rounded = f_rounded;

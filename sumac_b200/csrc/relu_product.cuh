@@ -73,6 +73,15 @@ __device__ unsigned long long g_sb_trace[28][512];
   } while (0)
 #endif
 
+// max over the p.nstats pairs of stats entry k (0: max_i |F_i|, 1: max |C|)
+struct ProductParams;
+__device__ __forceinline__ float stats_max(const unsigned int* stats, int nstats, int k) {
+  unsigned int m = 0u;
+#pragma unroll 4
+  for (int i = 0; i < nstats; ++i) m = max(m, stats[2 * i + k]);
+  return __uint_as_float(m);
+}
+
 struct ProductParams {
   int M;                 // rows of X
   int N;                 // rows of F (columns of C^T)
@@ -87,8 +96,11 @@ struct ProductParams {
   unsigned long long timeout_ns;
   // TF32 product mode: stats[0] = bits of max_i |F_i| (row norm), stats[1] = bits of max |C|;
   // Xg is X in global memory (row norms for the per-row scale of R).
+  // stats holds nstats such pairs (one per CTA of the launch that wrote them); the product takes
+  // their maxima (non-negative float bits compare as unsigned integers).
   const float* Xg;
   const unsigned int* stats;
+  int nstats;
   // product mode: 0 = R = ReLU(S); 1 = R = step(S) (1 where S > 0, else 0), the mask term of the
   // gradient of sum ReLU(A B^T) (relu_bat_reduce_jit/custom_op.py:74-82)
   int step;
@@ -597,8 +609,8 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
     int ec = 0;
     float fmax = 0.f;  // max_i |F_i| (row norms), for the row scales
     if constexpr (Cfg::H16) {
-      fmax = __uint_as_float(p.stats[0]);
-      const float cmax = __uint_as_float(p.stats[1]);
+      fmax = stats_max(p.stats, p.nstats, 0);
+      const float cmax = stats_max(p.stats, p.nstats, 1);
       int ex = 0;
       if (cmax > 0.f) frexpf(cmax, &ex);
       ec = 14 - ex;
@@ -863,7 +875,7 @@ __global__ void __launch_bounds__(ProductCfg<DP, BN, STAGES, X3, REDUCE, G>::THR
     float cscale = 1.f;
     const bool idle = REDUCE && p.f_rounded;  // nothing to prepare: the MMA waits the TMA
     if constexpr (Cfg::H16) {
-      const float cmax = __uint_as_float(p.stats[1]);
+      const float cmax = stats_max(p.stats, p.nstats, 1);
       int ex = 0;
       if (cmax > 0.f) frexpf(cmax, &ex);
       cscale = ldexpf(1.f, 14 - ex);
