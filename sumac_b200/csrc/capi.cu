@@ -337,9 +337,6 @@ struct SalsaPlan {
 static SalsaPlan plan_salsa(void* ws, int64_t M, int64_t b, int d, int Dp, bool x3, int sms) {
   Bump bp(ws);
   SalsaPlan p;
-  // [0] Gram-inverse done-CTA counter; from [2]: one (max |F_i|, max |C|) pair per gather CTA
-  // (the d > 32 path: one atomically maxed pair at [1..2])
-  p.counter = bp.take<unsigned int>(4 + 2 * (size_t)salsa_gather_ctas(b));
   p.ldct = round4(b);
   p.FI = bp.take<float>((size_t)b * Dp);
   p.Fhi = bp.take<float>((size_t)b * Dp);
@@ -351,6 +348,9 @@ static SalsaPlan plan_salsa(void* ws, int64_t M, int64_t b, int d, int Dp, bool 
   const size_t pbytes = d <= 32 ? salsa_ginv_scratch_bytes(b, d) : 0;
   p.gram = bp.take<double>(((gbytes > pbytes ? gbytes : pbytes) + 7) / 8);
   p.ginv = bp.take<float>((size_t)Dp * Dp);
+  // [0] Gram-inverse done-CTA counter; from [2]: one (max |F_i|, max |C|) pair per gather CTA
+  // (the d > 32 path: one atomically maxed pair at [1..2])
+  p.counter = bp.take<unsigned int>(4 + 2 * (size_t)salsa_gather_ctas(b));
   // the split count grows as b shrinks; size for the worst case over b' <= b
   int smax = 1;
   for (int64_t bb = b; bb > 0; bb = bb / 2) {
@@ -394,29 +394,13 @@ int sumac_salsa_block_update(const float* F, int64_t m_fixed, const int64_t* row
     // the finalize pass applies G^{-1}, which a side stream computes while the product runs
     SideStream* side = side_stream();
     if (!side) return fail(SUMAC_ERR_CUDA, "salsa_block_update: side stream creation failed");
-    // Where the product is short (few row tiles per SM, as on a rank of a sharded run) the Gram
-    // inverse is the longer branch: it then forks before the gather, reads the block rows through
-    // `rows` and gets its counter zeroed on the side stream. Otherwise it forks after the gather,
-    // reads the packed rows, and the gather zeroes its counter. Either way the gather writes every
-    // CTA's pair of operand maxima, so no memset sits on the main stream between block updates.
-    const int64_t row_tiles = (M + 127) / 128;
-    const bool early = row_tiles <= 4 * (int64_t)(sms > 2 * kGinvSms ? sms - kGinvSms : sms);
-    if (early) {
-      cudaEventRecord(side->fork, s);
-      cudaStreamWaitEvent(side->stream, side->fork, 0);
-      cudaMemsetAsync(p.counter, 0, sizeof(unsigned int), side->stream);
-      launch_salsa_ginv(F, rows, b, d, Dp, p.gram, p.counter, p.ginv, dev_err, side->stream);
-      cudaEventRecord(side->join, side->stream);
-    }
+    // no memset: the gather writes every CTA's pair of operand maxima and zeroes the counter
     launch_salsa_gather(F, rows, b, Dp, p.FI, p.Fhi, p.Flo, p.Cthi, p.Ctlo, p.ldct,
-                        x3 ? nullptr : p.counter + 2, early ? nullptr : p.counter, s);
-    if (!early) {
-      cudaEventRecord(side->fork, s);
-      cudaStreamWaitEvent(side->stream, side->fork, 0);
-      launch_salsa_ginv(p.FI, nullptr, b, d, Dp, p.gram, p.counter, p.ginv, dev_err,
-                        side->stream);
-      cudaEventRecord(side->join, side->stream);
-    }
+                        x3 ? nullptr : p.counter + 2, p.counter, s);
+    cudaEventRecord(side->fork, s);
+    cudaStreamWaitEvent(side->stream, side->fork, 0);
+    launch_salsa_ginv(p.FI, b, d, Dp, p.gram, p.counter, p.ginv, dev_err, side->stream);
+    cudaEventRecord(side->join, side->stream);
     // the product leaves kGinvSms SMs to the Gram-inverse launch, which then runs at full speed
     // instead of sharing issue slots with product CTAs
     const int psms = sms > 2 * kGinvSms ? sms - kGinvSms : sms;

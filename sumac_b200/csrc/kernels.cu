@@ -262,9 +262,7 @@ int salsa_gram_parts(int64_t b) { return cdiv64(b, PREP_ROWS) < 1 ? 1 : cdiv64(b
 // are needed only by the finalize pass: they are computed on a side stream while the product runs.
 //   salsa_gather_kernel  F_I = F[rows] (fp32, tf32 hi / lo halves), C^T = F_I^T (split in 3xTF32
 //                        mode) and the operand maxima of the TF32 product, 32 rows per CTA
-//   salsa_ginv_kernel    partial Grams (fp64) of the block rows (the gather's packed rows, or the
-//                        factor's rows through the row index, so that the launch need not wait
-//                        for the gather) split over at most kGinvSms CTAs;
+//   salsa_ginv_kernel    partial Grams (fp64) of the block rows split over at most kGinvSms CTAs;
 //                        the last CTA sums them in CTA order and inverts G by Gauss-Jordan
 //                        elimination (getrf's pivot choice): G^{-1} [Dp][Dp] (fp32, zero
 //                        outside d x d)
@@ -278,8 +276,7 @@ __global__ void __launch_bounds__(256) salsa_gather_kernel(
   __shared__ float wmax[2][8];
   pdl_wait();     // launched programmatically behind the previous block update
   pdl_trigger();  // the product may launch now; it waits for this grid before reading its output
-  // (when the Gram inverse of this update runs after this grid) zero its counter: the previous
-  // one has finished
+  // the Gram-inverse launch of this update runs after this grid; the previous one has finished
   if (blockIdx.x == 0 && threadIdx.x == 0 && ginv_counter) *ginv_counter = 0u;
   const int64_t r0 = (int64_t)blockIdx.x * 32;
   const int nr = (int)min((int64_t)32, b - r0);
@@ -412,7 +409,7 @@ __device__ __forceinline__ void warp_gauss_jordan16(const double (*a0)[32], int 
 
 template <int D>
 __global__ void __launch_bounds__(256) salsa_ginv_kernel(
-    const float* __restrict__ Ffix, const int64_t* __restrict__ rows, int64_t b, int d, int Dp, int64_t rows_per_cta,
+    const float* __restrict__ FI, int64_t b, int d, int Dp, int64_t rows_per_cta,
     double* __restrict__ parts, unsigned int* counter, double* __restrict__ LU,
     int* __restrict__ piv, float* __restrict__ ginv, int* err) {
   __shared__ float srow[PREP_ROWS * (D + 1)];
@@ -431,8 +428,7 @@ __global__ void __launch_bounds__(256) salsa_ginv_kernel(
     __syncthreads();
     for (int i = threadIdx.x; i < nr * D; i += blockDim.x) {
       const int rr = i / D, c = i - rr * D;
-      srow[rr * (D + 1) + c] =
-          c < d ? Ffix[(rows ? rows[c0 + rr] : c0 + rr) * Dp + c] : 0.f;
+      srow[rr * (D + 1) + c] = c < d ? FI[(c0 + rr) * Dp + c] : 0.f;
     }
     __syncthreads();
 #pragma unroll
@@ -547,7 +543,7 @@ void launch_salsa_gather(const float* Ffix, const int64_t* rows, int64_t b, int 
              rows, b, Dp, FI, Fhi, Flo, Cthi, Ctlo, ldct, stats, ginv_counter);
 }
 
-void launch_salsa_ginv(const float* Ffix, const int64_t* rows, int64_t b, int d, int Dp, void* scratch,
+void launch_salsa_ginv(const float* FI, int64_t b, int d, int Dp, void* scratch,
                        unsigned int* counter, float* ginv, int* err, cudaStream_t stream) {
   // at most kGinvSms CTAs (one per SM: a 256-thread CTA cannot share an SM with a product CTA),
   // on the SMs the concurrent fused product leaves free
@@ -558,10 +554,10 @@ void launch_salsa_ginv(const float* Ffix, const int64_t* rows, int64_t b, int d,
   int* piv = reinterpret_cast<int*>(LU + 32 * 32);
   count_launch();
   if (Dp == 16)
-    salsa_ginv_kernel<16><<<np, 256, 0, stream>>>(Ffix, rows, b, d, Dp, rpc, parts, counter, LU, piv,
+    salsa_ginv_kernel<16><<<np, 256, 0, stream>>>(FI, b, d, Dp, rpc, parts, counter, LU, piv,
                                                   ginv, err);
   else
-    salsa_ginv_kernel<32><<<np, 256, 0, stream>>>(Ffix, rows, b, d, Dp, rpc, parts, counter, LU, piv,
+    salsa_ginv_kernel<32><<<np, 256, 0, stream>>>(FI, b, d, Dp, rpc, parts, counter, LU, piv,
                                                   ginv, err);
 }
 

@@ -81,11 +81,9 @@ int salsa_gram_parts(int64_t b);
 
 // SALSA block step with C = F_I (d <= 32): gather F_I = Ffix[rows] (and its tf32 halves, its
 // transpose C^T = F_I^T split in 3xTF32 mode, and each CTA's operand maxima into its own pair
-// stats[2 * cta .. 2 * cta + 1], salsa_gather_ctas(b) pairs, no zeroing needed; it zeroes
-// ginv_counter when that is given) in one launch; G^{-1} of G = F_I^T F_I (rows Ffix[rows[i]], or
-// Ffix's first b rows when rows is null) into ginv [Dp][Dp] (fp32) in one launch whose last CTA
-// factors G (`counter` zero before the launch).
-// scratch: salsa_ginv_scratch_bytes(b, d).
+// stats[2 * cta .. 2 * cta + 1], salsa_gather_ctas(b) pairs, no zeroing needed) in one launch,
+// which also zeroes the Gram-inverse counter; then G^{-1} of G = F_I^T F_I into ginv [Dp][Dp]
+// (fp32) in one launch whose last CTA factors G. scratch: salsa_ginv_scratch_bytes(b, d).
 int salsa_gather_ctas(int64_t b);
 // SMs the Gram-inverse launch uses beside the fused product, which then runs on num_sms - kGinvSms
 constexpr int kGinvSms = 11;
@@ -93,7 +91,7 @@ size_t salsa_ginv_scratch_bytes(int64_t b, int d);
 void launch_salsa_gather(const float* Ffix, const int64_t* rows, int64_t b, int Dp, float* FI,
                          float* Fhi, float* Flo, float* Cthi, float* Ctlo, int64_t ldct,
                          unsigned int* stats, unsigned int* ginv_counter, cudaStream_t stream);
-void launch_salsa_ginv(const float* Ffix, const int64_t* rows, int64_t b, int d, int Dp, void* scratch,
+void launch_salsa_ginv(const float* FI, int64_t b, int d, int Dp, void* scratch,
                        unsigned int* counter, float* ginv, int* err, cudaStream_t stream);
 
 // Row exchange over NVLink peer memory (see kernels.cu): the owned rows of rows[0..nrows) into
