@@ -99,7 +99,9 @@ def test_block_csr_bit_exact(m_fixed, M, nb, nnz):
 
 
 @pytest.mark.parametrize("prec", PRECS)
+# M = 80000: more row tiles than two per SM, as at C4
 @pytest.mark.parametrize("d,m_fixed,b,M,nnz", [(16, 5000, 1393, 4000, 30000), (6, 400, 100, 90, 900),
+                                               (16, 5000, 1393, 80000, 200000),
                                                (32, 3000, 300, 2500, 20000), (64, 2000, 500, 700, 5000),
                                                (128, 1500, 400, 600, 4000)])
 def test_salsa_block_update(d, m_fixed, b, M, nnz, prec):
