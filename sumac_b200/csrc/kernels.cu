@@ -743,9 +743,10 @@ __global__ void __launch_bounds__(256, 3) finalize_kernel(FinalizeArgs a) {
                                 __shfl_sync(0xffffffffu, x[v].z, sl), __shfl_sync(0xffffffffu, x[v].w, sl));
             hcor[v] = make_float4(0.f, 0.f, 0.f, 0.f);
           }
-          // HU entries per lane group and round (entry q0 + u * RPW + gw), the next round's
+          // HU entries per lane group and round (entry q0 + u * RPW + gw; 2 measured faster than 1
+          // or 4: 20.2 against 21.3 / 21.1 us at C4), the next round's
           // entries loaded before this round's F / C gathers
-          constexpr int HU = 4;
+          constexpr int HU = 2;
           int2 en[HU];
 #pragma unroll
           for (int u = 0; u < HU; ++u) {
